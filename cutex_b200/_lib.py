@@ -1,0 +1,145 @@
+"""ctypes binding of libcutex_mxfp8.so (the C ABI declared in include/cutex_mxfp8.h).
+
+The library is loaded from ``cutex_b200/_lib`` (built in-tree by
+``cutex_b200.build``). There is no fallback: if the library is missing or
+fails to load, every GEMM/quantiser call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+from .build import LIB_PATH
+
+CUTEX_OK = 0
+CUTEX_ERR_INVALID_ARGUMENT = 1
+CUTEX_ERR_SHAPE = 2
+CUTEX_ERR_ALIGN = 3
+CUTEX_ERR_UNSUPPORTED_DEVICE = 4
+CUTEX_ERR_CUDA = 5
+CUTEX_ERR_TIMEOUT = 6
+CUTEX_ERR_WORKSPACE = 7
+
+KERNEL_AUTO = 0
+KERNEL_1CTA = 1
+KERNEL_2CTA = 2
+KERNEL_SKINNY = 3
+
+
+class GemmConfigC(ctypes.Structure):
+    _fields_ = [
+        ("kernel", ctypes.c_int32),
+        ("tile_n", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("raster_group", ctypes.c_int32),
+        ("raster_along_n", ctypes.c_int32),
+        ("split_k", ctypes.c_int32),
+        ("max_ctas", ctypes.c_int32),
+        ("epi_buffers", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 8),
+    ]
+
+
+class GemmInfoC(ctypes.Structure):
+    _fields_ = [
+        ("kernel", ctypes.c_int32),
+        ("tile_m", ctypes.c_int32),
+        ("tile_n", ctypes.c_int32),
+        ("tile_k", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("cluster_size", ctypes.c_int32),
+        ("grid_ctas", ctypes.c_int32),
+        ("smem_bytes", ctypes.c_int32),
+        ("num_tiles", ctypes.c_int32),
+        ("split_k", ctypes.c_int32),
+        ("epi_buffers", ctypes.c_int32),
+        ("raster_group", ctypes.c_int32),
+        ("workspace_bytes", ctypes.c_int64),
+    ]
+
+
+class CutexError(RuntimeError):
+    """A non-zero cutex_status returned by the native library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class CutexArgumentError(CutexError, ValueError):
+    """Shape, alignment or configuration rejected by the library (a ValueError, as in the reference)."""
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+
+# Exported symbol -> (restype, argtypes). Kept in the same order as include/cutex_mxfp8.h.
+SIGNATURES = {
+    "cutex_mxfp8_gemm": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.POINTER(GemmConfigC), _vp, _i64, _vp],
+    ),
+    "cutex_mxfp8_query": (
+        ctypes.c_int,
+        [ctypes.POINTER(GemmConfigC), _i64, _i64, _i64, ctypes.POINTER(GemmInfoC)],
+    ),
+    "cutex_dense_gemm_v13": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _vp]),
+    "cutex_mxfp8_quantize": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "cutex_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "cutex_last_device_status": (ctypes.c_int, [_vp]),
+    "cutex_device_sm_count": (ctypes.c_int, [ctypes.POINTER(_i32)]),
+    "cutex_version": (ctypes.c_char_p, []),
+}
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the native library; raise if it is not built."""
+
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"cutex_b200 native library not found at {LIB_PATH}; "
+                    "build it with `python -m cutex_b200.build` (there is no CPU fallback)"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = lib
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return load().cutex_status_string(int(status)).decode()
+
+
+def check(status: int, what: str) -> None:
+    if status == CUTEX_OK:
+        return
+    msg = f"{what}: {status_string(status)}"
+    if status in (CUTEX_ERR_INVALID_ARGUMENT, CUTEX_ERR_SHAPE, CUTEX_ERR_ALIGN, CUTEX_ERR_WORKSPACE):
+        raise CutexArgumentError(status, msg)
+    raise CutexError(status, msg)
+
+
+def make_config(**fields) -> GemmConfigC:
+    cfg = GemmConfigC()
+    for name, value in fields.items():
+        if name not in {f[0] for f in GemmConfigC._fields_} or name == "reserved":
+            raise ValueError(f"unknown GEMM config field {name!r}")
+        setattr(cfg, name, int(value))
+    return cfg
+
+
+def version() -> str:
+    return load().cutex_version().decode()

@@ -1,0 +1,407 @@
+// Host side of libcutex_mxfp8.so: argument validation, configuration
+// resolution, TMA descriptor encoding and kernel launch for the C ABI in
+// include/cutex_mxfp8.h. Nothing here allocates device memory or
+// synchronises a stream (except cutex_last_device_status, by contract).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/cutex_mxfp8.h"
+#include "mxfp8_gemm.cuh"
+#include "mxfp8_quant.cuh"
+
+namespace cutex {
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int64_t kMaxDim = (int64_t{1} << 31) - 1;
+
+struct DeviceState {
+  bool ready = false;
+  int status = CUTEX_OK;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+};
+
+std::mutex g_mutex;
+DeviceState g_devices[kMaxDevices];
+
+int current_device_state(DeviceState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CUTEX_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState& st = g_devices[dev];
+  if (!st.ready) {
+    if (cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&st.cc_major, cudaDevAttrComputeCapabilityMajor, dev) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&st.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) !=
+            cudaSuccess) {
+      return CUTEX_ERR_CUDA;
+    }
+    st.status = (st.cc_major == 10 && st.cc_minor == 0) ? CUTEX_OK : CUTEX_ERR_UNSUPPORTED_DEVICE;
+    st.ready = true;
+  }
+  *out = &st;
+  return st.status;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+bool encode(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* ptr,
+            const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+            CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promo) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5];
+  cuuint32_t e[5];
+  for (uint32_t i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) s[i] = strides_bytes[i];
+  }
+  return fn(map, dtype, rank, const_cast<void*>(ptr), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swizzle, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// K-major e4m3 operand [rows, K] read in (box_rows x 128) tiles, 128-byte swizzle.
+bool encode_operand(CUtensorMap* map, const void* p, int64_t rows, int64_t K, uint32_t box_rows) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(K)};
+  const uint32_t box[2] = {128u, box_rows};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p, dims, strides, box,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+}
+
+// Swizzled scales viewed as [row blocks][K/128][128 x u32]: one 512-byte chunk
+// per (128-row block, 128-K stage); `blocks` consecutive row blocks per load.
+bool encode_scales(CUtensorMap* map, const void* p, int64_t rows, int64_t K, uint32_t blocks) {
+  const int64_t row_blocks = (rows + 127) / 128;
+  const uint64_t dims[3] = {128u, static_cast<uint64_t>(K / 128), static_cast<uint64_t>(row_blocks)};
+  const uint64_t strides[2] = {512u, static_cast<uint64_t>(K / 128) * 512u};
+  const uint32_t box[3] = {128u, 1u, blocks};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, p, dims, strides, box,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+}
+
+// bf16 output [M, N] with row stride ldd, written in 32 x 64 boxes.
+bool encode_output(CUtensorMap* map, void* p, int64_t M, int64_t N, int64_t ldd) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ldd) * 2u};
+  const uint32_t box[2] = {64u, 32u};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p, dims, strides, box,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+}
+
+// ------------------------------------------------------------ kernel registry
+
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap,
+                          GemmArgs);
+
+struct Variant {
+  int cta_group, tile_n, stages, epi_bufs, smem_bytes;
+  const void* fn;
+  bool attr_set[kMaxDevices];
+  int max_clusters[kMaxDevices];
+};
+
+template <int CG, int BN, int S, int E>
+Variant make_variant() {
+  Variant v{};
+  v.cta_group = CG;
+  v.tile_n = BN;
+  v.stages = S;
+  v.epi_bufs = E;
+  v.smem_bytes = GemmCfg<CG, BN, S, E>::kSmemBytes;
+  v.fn = reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E>);
+  return v;
+}
+
+Variant g_variants[] = {
+    make_variant<1, 128, 4, 2>(), make_variant<1, 128, 5, 2>(), make_variant<1, 128, 6, 1>(),
+    make_variant<1, 256, 3, 2>(), make_variant<1, 256, 4, 1>(), make_variant<2, 256, 4, 2>(),
+    make_variant<2, 256, 5, 2>(), make_variant<2, 256, 6, 1>(),
+};
+
+Variant* find_variant(int cg, int bn, int stages, int epi) {
+  Variant* best = nullptr;
+  for (auto& v : g_variants) {
+    if (v.cta_group != cg || v.tile_n != bn) continue;
+    if (stages != 0 && v.stages != stages) continue;
+    if (epi != 0 && v.epi_bufs != epi) continue;
+    // Default: deepest ring, then the most epilogue buffers.
+    if (best == nullptr || v.stages > best->stages ||
+        (v.stages == best->stages && v.epi_bufs > best->epi_bufs))
+      best = &v;
+  }
+  return best;
+}
+
+struct Plan {
+  Variant* variant;
+  int kernel;
+  int tile_n;
+  int raster_group;
+  int raster_along_n;
+  int grid_ctas;
+  int num_m_tiles, num_n_tiles, num_tiles;
+};
+
+bool cfg_reserved_zero(const cutex_gemm_config* cfg) {
+  for (int r : cfg->reserved)
+    if (r != 0) return false;
+  return true;
+}
+
+int validate_shape(int64_t M, int64_t N, int64_t K) {
+  if (M < 1 || N < 1 || K < 1) return CUTEX_ERR_SHAPE;
+  if (M > kMaxDim || N > kMaxDim || K > kMaxDim) return CUTEX_ERR_SHAPE;
+  if (K % 128 != 0 || N % 16 != 0) return CUTEX_ERR_ALIGN;
+  return CUTEX_OK;
+}
+
+int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t K, int sm_count,
+                 Plan* plan) {
+  cutex_gemm_config cfg{};
+  if (cfg_in != nullptr) {
+    cfg = *cfg_in;
+    if (!cfg_reserved_zero(&cfg)) return CUTEX_ERR_INVALID_ARGUMENT;
+  }
+  if (cfg.kernel < 0 || cfg.kernel > CUTEX_KERNEL_SKINNY || cfg.stages < 0 || cfg.raster_group < 0 ||
+      cfg.max_ctas < 0 || cfg.split_k < 0 || cfg.epi_buffers < 0 || cfg.epi_buffers > 2 ||
+      (cfg.raster_along_n != 0 && cfg.raster_along_n != 1))
+    return CUTEX_ERR_INVALID_ARGUMENT;
+  if (cfg.tile_n != 0 && cfg.tile_n != 128 && cfg.tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
+  int kernel = cfg.kernel;
+  if (kernel == CUTEX_KERNEL_SKINNY) return CUTEX_ERR_INVALID_ARGUMENT;  // not built yet
+  if (kernel == CUTEX_KERNEL_AUTO) kernel = (M > 128 && N % 256 == 0) ? CUTEX_KERNEL_2CTA : CUTEX_KERNEL_1CTA;
+  int tile_n = cfg.tile_n;
+  if (kernel == CUTEX_KERNEL_2CTA) {
+    if (tile_n == 0) tile_n = 256;
+    if (tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
+  } else if (tile_n == 0) {
+    tile_n = (N % 256 == 0 && M > 128) ? 256 : 128;
+  }
+  const int cg = kernel == CUTEX_KERNEL_2CTA ? 2 : 1;
+  Variant* v = find_variant(cg, tile_n, cfg.stages, cfg.epi_buffers);
+  if (v == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  plan->variant = v;
+  plan->kernel = kernel;
+  plan->tile_n = tile_n;
+  plan->num_m_tiles = static_cast<int>((M + 128 * cg - 1) / (128 * cg));
+  plan->num_n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
+  const int64_t tiles = static_cast<int64_t>(plan->num_m_tiles) * plan->num_n_tiles;
+  if (tiles > kMaxDim) return CUTEX_ERR_SHAPE;
+  plan->num_tiles = static_cast<int>(tiles);
+  plan->raster_group = cfg.raster_group != 0 ? cfg.raster_group : 8;
+  plan->raster_along_n = cfg.raster_along_n;
+  int units = sm_count / cg;  // persistent CTAs (pairs) that fit, one per SM
+  if (cfg.max_ctas != 0) units = std::min(units, std::max(1, cfg.max_ctas / cg));
+  units = std::max(1, std::min(units, plan->num_tiles));
+  plan->grid_ctas = units * cg;
+  return CUTEX_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const void* sfa,
+                const void* sfb, void* d, int64_t M, int64_t N, int64_t K, int64_t ldd,
+                cudaStream_t stream) {
+  Variant* v = plan.variant;
+  const int cg = v->cta_group;
+  CUtensorMap ta, tb, tsa, tsb, td;
+  if (!encode_operand(&ta, a, M, K, 128) || !encode_operand(&tb, b, N, K, v->tile_n / cg) ||
+      !encode_scales(&tsa, sfa, M, K, 1) || !encode_scales(&tsb, sfb, N, K, v->tile_n / 128) ||
+      !encode_output(&td, d, M, N, ldd))
+    return CUTEX_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!v->attr_set[dev]) {
+      if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               v->smem_bytes) != cudaSuccess)
+        return CUTEX_ERR_CUDA;
+      v->attr_set[dev] = true;
+    }
+  }
+  GemmArgs args{};
+  args.num_m_tiles = plan.num_m_tiles;
+  args.num_n_tiles = plan.num_n_tiles;
+  args.num_tiles = plan.num_tiles;
+  args.num_k_blocks = static_cast<int>(K / 128);
+  args.raster_group = plan.raster_group;
+  args.raster_along_n = plan.raster_along_n;
+
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(static_cast<unsigned>(plan.grid_ctas), 1, 1);
+  lc.blockDim = dim3(192, 1, 1);
+  lc.dynamicSmemBytes = static_cast<size_t>(v->smem_bytes);
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (cg == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    // A persistent grid must be co-resident: cap it at the number of CTA pairs
+    // the GPCs can hold at once (queried once per device and variant).
+    int max_clusters = 0;
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      max_clusters = v->max_clusters[dev];
+    }
+    if (max_clusters == 0) {
+      if (cudaOccupancyMaxActiveClusters(&max_clusters, v->fn, &lc) != cudaSuccess ||
+          max_clusters < 1)
+        return CUTEX_ERR_CUDA;
+      std::lock_guard<std::mutex> lock(g_mutex);
+      v->max_clusters[dev] = max_clusters;
+    }
+    if (plan.grid_ctas > 2 * max_clusters) lc.gridDim.x = static_cast<unsigned>(2 * max_clusters);
+  }
+  void* params[] = {&ta, &tb, &tsa, &tsb, &td, &args};
+  if (cudaLaunchKernelExC(&lc, v->fn, params) != cudaSuccess) return CUTEX_ERR_CUDA;
+  return CUTEX_OK;
+}
+
+}  // namespace
+}  // namespace cutex
+
+using namespace cutex;
+
+extern "C" int cutex_mxfp8_query(const cutex_gemm_config* cfg, int64_t M, int64_t N, int64_t K,
+                                 cutex_gemm_info* info) {
+  if (info == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  const int st = validate_shape(M, N, K);
+  if (st != CUTEX_OK) return st;
+  int sm_count = 148;
+  DeviceState* ds = nullptr;
+  if (current_device_state(&ds) == CUTEX_OK) sm_count = ds->sm_count;
+  Plan plan{};
+  const int rc = resolve_plan(cfg, M, N, K, sm_count, &plan);
+  if (rc != CUTEX_OK) return rc;
+  std::memset(info, 0, sizeof(*info));
+  info->kernel = plan.kernel;
+  info->tile_m = 128 * plan.variant->cta_group;
+  info->tile_n = plan.tile_n;
+  info->tile_k = 128;
+  info->stages = plan.variant->stages;
+  info->cluster_size = plan.variant->cta_group;
+  info->grid_ctas = plan.grid_ctas;
+  info->smem_bytes = plan.variant->smem_bytes;
+  info->num_tiles = plan.num_tiles;
+  info->split_k = 1;
+  info->epi_buffers = plan.variant->epi_bufs;
+  info->raster_group = plan.raster_group;
+  info->workspace_bytes = 0;
+  return CUTEX_OK;
+}
+
+extern "C" int cutex_mxfp8_gemm(const void* a, const void* b, const void* sfa, const void* sfb,
+                                void* d, int64_t M, int64_t N, int64_t K, int64_t ldd,
+                                const cutex_gemm_config* cfg, void* workspace,
+                                int64_t workspace_bytes, cutex_stream_t stream) {
+  (void)workspace;
+  if (a == nullptr || b == nullptr || sfa == nullptr || sfb == nullptr || d == nullptr)
+    return CUTEX_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < 0) return CUTEX_ERR_INVALID_ARGUMENT;
+  int st = validate_shape(M, N, K);
+  if (st != CUTEX_OK) return st;
+  if (ldd < N || ldd % 8 != 0 || ldd > kMaxDim) return CUTEX_ERR_ALIGN;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(sfa) || !aligned16(sfb) || !aligned16(d))
+    return CUTEX_ERR_ALIGN;
+  DeviceState* ds = nullptr;
+  st = current_device_state(&ds);
+  if (st != CUTEX_OK) return st;
+  Plan plan{};
+  st = resolve_plan(cfg, M, N, K, ds->sm_count, &plan);
+  if (st != CUTEX_OK) return st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
+  return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd,
+                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cutex_dense_gemm_v13(const void* a, const void* b, const void* sfa, const void* sfb,
+                                    void* c, int32_t max_active_clusters, cutex_stream_t stream) {
+  cutex_gemm_config cfg{};
+  cfg.kernel = CUTEX_KERNEL_2CTA;
+  cfg.tile_n = 256;
+  cfg.max_ctas = max_active_clusters > 0 ? 2 * max_active_clusters : 0;
+  const int64_t n = 16384;
+  return cutex_mxfp8_gemm(a, b, sfa, sfb, c, n, n, n, n, &cfg, nullptr, 0, stream);
+}
+
+extern "C" int cutex_mxfp8_quantize(const void* x, int32_t x_dtype, int64_t rows, int64_t K,
+                                    int64_t ldx, void* q, void* sf, cutex_stream_t stream) {
+  if (x == nullptr || q == nullptr || sf == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  if (x_dtype != 0 && x_dtype != 1) return CUTEX_ERR_INVALID_ARGUMENT;
+  if (rows < 1 || K < 1 || rows > kMaxDim || K > kMaxDim) return CUTEX_ERR_SHAPE;
+  if (K % 128 != 0 || ldx < K || ldx % 8 != 0) return CUTEX_ERR_ALIGN;
+  if (!aligned16(x) || !aligned16(q) || !aligned16(sf)) return CUTEX_ERR_ALIGN;
+  DeviceState* ds = nullptr;
+  const int st = current_device_state(&ds);
+  if (st != CUTEX_OK) return st;
+  return launch_quantize(x, x_dtype, rows, K, ldx, q, sf, ds->sm_count,
+                         reinterpret_cast<cudaStream_t>(stream))
+             ? CUTEX_OK
+             : CUTEX_ERR_CUDA;
+}
+
+extern "C" const char* cutex_status_string(int status) {
+  switch (status) {
+    case CUTEX_OK: return "CUTEX_OK";
+    case CUTEX_ERR_INVALID_ARGUMENT: return "CUTEX_ERR_INVALID_ARGUMENT: invalid argument or configuration";
+    case CUTEX_ERR_SHAPE: return "CUTEX_ERR_SHAPE: unsupported problem shape";
+    case CUTEX_ERR_ALIGN: return "CUTEX_ERR_ALIGN: pointer, stride or K alignment rule violated";
+    case CUTEX_ERR_UNSUPPORTED_DEVICE: return "CUTEX_ERR_UNSUPPORTED_DEVICE: requires compute capability 10.0 (B200)";
+    case CUTEX_ERR_CUDA: return "CUTEX_ERR_CUDA: CUDA runtime or driver call failed";
+    case CUTEX_ERR_TIMEOUT: return "CUTEX_ERR_TIMEOUT: device-side wait exceeded its limit";
+    case CUTEX_ERR_WORKSPACE: return "CUTEX_ERR_WORKSPACE: workspace missing or too small";
+    default: return "CUTEX_ERR_UNKNOWN";
+  }
+}
+
+extern "C" int cutex_last_device_status(cutex_stream_t stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int value = 0;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return CUTEX_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&value, g_cutex_device_status, sizeof(int)) != cudaSuccess)
+    return CUTEX_ERR_CUDA;
+  if (value != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_cutex_device_status, &zero, sizeof(int)) != cudaSuccess)
+      return CUTEX_ERR_CUDA;
+    return CUTEX_ERR_TIMEOUT;
+  }
+  return CUTEX_OK;
+}
+
+extern "C" int cutex_device_sm_count(int32_t* sm_count) {
+  if (sm_count == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  DeviceState* ds = nullptr;
+  const int st = current_device_state(&ds);
+  if (ds == nullptr) return st;
+  *sm_count = ds->sm_count;
+  return st;
+}
+
+extern "C" const char* cutex_version(void) { return "cutex-b200 0.1.0 sm_100a"; }

@@ -1,0 +1,379 @@
+// Persistent, warp-specialised MXFP8 block-scaled GEMM for sm_100a.
+//
+//   D[M,N] bf16 = (A[M,K] e4m3 * SFA) . (B[N,K] e4m3 * SFB)^T, FP32 accumulate.
+//
+// One CTA (kCtaGroup = 1) or one CTA pair (kCtaGroup = 2, cluster of 2) owns a
+// (128*kCtaGroup) x kTileN output tile at a time and walks a static,
+// grouped-raster sequence of tiles (persistent grid sized to the SM count).
+//
+// Warp roles (192 threads):
+//   warps 0-3  epilogue: TMEM -> registers -> BF16 -> swizzled SMEM -> TMA store.
+//              Warp w owns TMEM lanes [32w, 32w+32), i.e. output rows 32w..32w+31.
+//   warp 4     MMA issuer (one thread; the pair leader only when kCtaGroup = 2):
+//              per K-stage copies the SFA/SFB chunks SMEM->TMEM (tcgen05.cp) and
+//              issues four K=32 block-scaled MMAs, then commits the stage back.
+//   warp 5     TMA producer (one thread per CTA): A, B, SFA, SFB tiles into a
+//              kStages-deep ring guarded by full/empty mbarriers.
+//
+// TMEM plan (512 columns, 32-bit): two accumulator buffers alternate by tile.
+// When two full buffers plus the 16 scale-factor columns do not fit (tile_n =
+// 256), buffer 1 starts at column 240 and overlaps the last 16 columns of
+// buffer 0; the epilogue reads the overlapping 64-column chunk first and then
+// releases the accumulator, so the next tile's MMAs start while the rest of
+// the tile is still being stored. Scale factors: SFA 4 columns (128 rows),
+// SFB 4 columns per 128 rows of N, byte k of a column = K-block k of a stage.
+//
+// K-stage: 128 K values. A stage holds the A tile (128 x 128 B), this CTA's B
+// rows (kTileN/kCtaGroup x 128 B), the 512-byte SFA chunk and the full SFB
+// chunk(s) of the MMA's N (each CTA of a pair loads its own copy; no
+// cluster-multicast loads are used anywhere).
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "ptx.cuh"
+
+namespace cutex {
+
+// Device-side error word; the first kernel error (e.g. a wait timeout) wins.
+// The library is a single translation unit, so the header defines it.
+__device__ int g_cutex_device_status = 0;
+
+enum DeviceError : int {
+  kDevOk = 0,
+  kDevTimeoutProducer = 0x101,
+  kDevTimeoutMma = 0x102,
+  kDevTimeoutEpilogue = 0x103,
+  kDevTimeoutAccEmpty = 0x104,
+};
+
+struct GemmArgs {
+  int num_m_tiles;  // output tiles along M (tile rows = 128 * kCtaGroup)
+  int num_n_tiles;  // output tiles along N
+  int num_tiles;
+  int num_k_blocks;  // K / 128
+  int raster_group;
+  int raster_along_n;
+};
+
+constexpr int kSmemLimit = 232448;  // max dynamic shared memory per block on sm_100
+
+constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs>
+struct GemmCfg {
+  static constexpr int kThreads = 192;
+  static constexpr int kTileM = 128;  // rows per CTA
+  static constexpr int kTileK = 128;  // K values (bytes) per stage
+  static constexpr int kLoadN = kTileN / kCtaGroup;  // B rows each CTA loads
+  static constexpr int kABytes = kTileM * kTileK;
+  static constexpr int kBBytes = kLoadN * kTileK;
+  static constexpr int kSFABytes = 512;
+  static constexpr int kSFBBytes = (kTileN / 128) * 512;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSFABytes + kSFBBytes;
+  static constexpr uint32_t kTxBytes = kStageBytes * kCtaGroup;
+
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + kStages * kABytes;
+  static constexpr int kOffSFA = kOffB + kStages * kBBytes;
+  static constexpr int kOffSFB = kOffSFA + kStages * kSFABytes;
+  static constexpr int kOffC = align_up(kOffSFB + kStages * kSFBBytes, 1024);
+  static constexpr int kCBufBytes = 32 * 64 * 2;  // 32 rows x 64 bf16, 128B-swizzled
+  static constexpr int kOffBar = kOffC + 4 * kEpiBufs * kCBufBytes;
+  static constexpr int kNumBars = 2 * kStages + 4;
+  static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + base alignment slack
+
+  static constexpr int kTmemCols = 512;
+  static constexpr int kSFACols = 4;
+  static constexpr int kSFBCols = (kTileN / 128) * 4;
+  static constexpr int kSFReserved = 16;
+  static constexpr bool kOverlap = 2 * kTileN + kSFReserved > kTmemCols;
+  static constexpr int kAcc1Col = kOverlap ? (kTmemCols - kSFReserved - kTileN) : kTileN;
+  static constexpr int kSFACol = kOverlap ? (kTmemCols - kSFReserved) : 2 * kTileN;
+  static constexpr int kSFBCol = kSFACol + kSFACols;
+  static constexpr int kChunks = kTileN / 64;
+  // First 64-column chunk the epilogue reads from buffer 0 / buffer 1.
+  static constexpr int kFirstChunk0 = kOverlap ? kAcc1Col / 64 : 0;
+  static constexpr uint32_t kIdesc = ptx::mxf8_idesc(kTileM * kCtaGroup, kTileN);
+
+  static_assert(kCtaGroup == 1 || kCtaGroup == 2, "cta group");
+  static_assert(kTileN == 128 || kTileN == 256, "tile_n");
+  static_assert(kCtaGroup == 1 || kTileN == 256, "the CTA-pair kernel uses tile_n = 256");
+  static_assert(kSFACols + kSFBCols <= kSFReserved, "scale-factor columns");
+  static_assert(kSFBCol + kSFBCols <= kTmemCols, "TMEM plan");
+  static_assert(!kOverlap || (kTileN - kAcc1Col) <= 64 - (kAcc1Col % 64),
+                "overlap must sit inside one epilogue chunk");
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
+  static_assert(kEpiBufs == 1 || kEpiBufs == 2, "epilogue buffers");
+};
+
+__device__ __forceinline__ void tile_coords(int t, const GemmArgs& a, int& mt, int& nt) {
+  const int g_size = a.raster_group;
+  if (!a.raster_along_n) {
+    const int per_group = g_size * a.num_n_tiles;
+    const int g = t / per_group;
+    const int r = t - g * per_group;
+    const int m0 = g * g_size;
+    const int gm = min(g_size, a.num_m_tiles - m0);
+    mt = m0 + r % gm;
+    nt = r / gm;
+  } else {
+    const int per_group = g_size * a.num_m_tiles;
+    const int g = t / per_group;
+    const int r = t - g * per_group;
+    const int n0 = g * g_size;
+    const int gn = min(g_size, a.num_n_tiles - n0);
+    nt = n0 + r % gn;
+    mt = r / gn;
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(lo), __uint_as_float(hi));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+// Wait ~50 us so that TMA loads already in flight land before the CTA exits on
+// an error path (loads of valid addresses complete on their own).
+__device__ __forceinline__ void settle_inflight_copies() {
+  const uint64_t t0 = ptx::globaltimer();
+  while (ptx::globaltimer() - t0 < 50000ull) __nanosleep(1000);
+}
+
+template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs>
+__global__ void __launch_bounds__(192, 1)
+    mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                      const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_sfa,
+                      const __grid_constant__ CUtensorMap tmap_sfb,
+                      const __grid_constant__ CUtensorMap tmap_d, const GemmArgs args) {
+  using C = GemmCfg<kCtaGroup, kTileN, kStages, kEpiBufs>;
+  constexpr bool kPair = kCtaGroup == 2;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = ptx::smem_u32(smem_raw);
+  const uint32_t smem = (raw_base + 1023u) & ~1023u;
+  uint8_t* smem_ptr = smem_raw + (smem - raw_base);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = ptx::lane_id();
+  const uint32_t rank = kPair ? ptx::cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x / kCtaGroup;
+  const int num_clusters = gridDim.x / kCtaGroup;
+  int* status = &g_cutex_device_status;
+
+  const uint32_t bar0 = smem + C::kOffBar;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
+  auto acc_full_bar = [&](int b) { return bar0 + 8u * (2 * kStages + b); };
+  auto acc_empty_bar = [&](int b) { return bar0 + 8u * (2 * kStages + 2 + b); };
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem_ptr + C::kOffTmemSlot);
+
+  if (warp == 5 && lane == 0) {
+    ptx::prefetch_tmap(&tmap_a);
+    ptx::prefetch_tmap(&tmap_b);
+    ptx::prefetch_tmap(&tmap_sfa);
+    ptx::prefetch_tmap(&tmap_sfb);
+    ptx::prefetch_tmap(&tmap_d);
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(full_bar(s), 1);
+      ptx::mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(acc_full_bar(b), 1);
+      ptx::mbar_init(acc_empty_bar(b), 4 * kCtaGroup);
+    }
+    ptx::fence_mbar_init();
+  }
+  if (warp == 4) {
+    ptx::tmem_alloc<kCtaGroup>(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)), C::kTmemCols);
+    ptx::tmem_relinquish<kCtaGroup>();
+  }
+  ptx::tc_fence_before();
+  if constexpr (kPair) ptx::cluster_sync(); else __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 5) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t kit = 0;
+      bool ok = true;
+      for (int t = cluster_id; ok && t < args.num_tiles; t += num_clusters) {
+        int mt, nt;
+        tile_coords(t, args, mt, nt);
+        const int a_row = mt * (128 * kCtaGroup) + static_cast<int>(rank) * 128;
+        const int b_row = nt * kTileN + static_cast<int>(rank) * C::kLoadN;
+        const int sfa_blk = a_row / 128;
+        const int sfb_blk = (nt * kTileN) / 128;
+        for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
+          const int s = static_cast<int>(kit % kStages);
+          const uint32_t round = kit / kStages;
+          if (!ptx::mbar_wait(empty_bar(s), (round & 1u) ^ 1u, status, kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (leader) ptx::mbar_arrive_expect_tx(full_bar(s), C::kTxBytes);
+          const uint32_t sa = smem + C::kOffA + s * C::kABytes;
+          const uint32_t sb = smem + C::kOffB + s * C::kBBytes;
+          const uint32_t ssfa = smem + C::kOffSFA + s * C::kSFABytes;
+          const uint32_t ssfb = smem + C::kOffSFB + s * C::kSFBBytes;
+          const int kx = kb * 128;
+          if constexpr (kPair) {
+            const uint32_t fb = ptx::mapa(full_bar(s), 0);
+            ptx::tma_load_2d_pair(sa, &tmap_a, fb, kx, a_row, ptx::kEvictNormal);
+            ptx::tma_load_2d_pair(sb, &tmap_b, fb, kx, b_row, ptx::kEvictNormal);
+            ptx::tma_load_3d_pair(ssfa, &tmap_sfa, fb, 0, kb, sfa_blk, ptx::kEvictNormal);
+            ptx::tma_load_3d_pair(ssfb, &tmap_sfb, fb, 0, kb, sfb_blk, ptx::kEvictNormal);
+          } else {
+            const uint32_t fb = full_bar(s);
+            ptx::tma_load_2d(sa, &tmap_a, fb, kx, a_row, ptx::kEvictNormal);
+            ptx::tma_load_2d(sb, &tmap_b, fb, kx, b_row, ptx::kEvictNormal);
+            ptx::tma_load_3d(ssfa, &tmap_sfa, fb, 0, kb, sfa_blk, ptx::kEvictNormal);
+            ptx::tma_load_3d(ssfb, &tmap_sfb, fb, 0, kb, sfb_blk, ptx::kEvictNormal);
+          }
+        }
+      }
+      // Drain: every stage this CTA filled has been consumed by the MMAs.
+      for (int i = 0; ok && i < kStages; ++i) {
+        const uint32_t k2 = kit + i;
+        ok = ptx::mbar_wait(empty_bar(static_cast<int>(k2 % kStages)),
+                            ((k2 / kStages) & 1u) ^ 1u, status, kDevTimeoutProducer);
+      }
+      if (!ok) settle_inflight_copies();
+    }
+    __syncwarp();
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ MMA issuer
+    if (leader && lane == 0) {
+      uint32_t kit = 0;
+      bool ok = true;
+      int it = 0;
+      const uint32_t sfa_t = tmem_base + C::kSFACol;
+      const uint32_t sfb_t = tmem_base + C::kSFBCol;
+      for (int t = cluster_id; ok && t < args.num_tiles; t += num_clusters, ++it) {
+        const int buf = it & 1;
+        if constexpr (C::kOverlap) {
+          if (it >= 1)
+            ok = ptx::mbar_wait<kPair>(acc_empty_bar((it - 1) & 1), ((it - 1) >> 1) & 1, status,
+                                       kDevTimeoutAccEmpty);
+        } else {
+          if (it >= 2)
+            ok = ptx::mbar_wait<kPair>(acc_empty_bar(buf), ((it - 2) >> 1) & 1, status,
+                                       kDevTimeoutAccEmpty);
+        }
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const uint32_t d_t = tmem_base + (buf ? C::kAcc1Col : 0);
+        for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
+          const int s = static_cast<int>(kit % kStages);
+          if (!ptx::mbar_wait(full_bar(s), (kit / kStages) & 1u, status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sa = smem + C::kOffA + s * C::kABytes;
+          const uint32_t sb = smem + C::kOffB + s * C::kBBytes;
+          const uint32_t ssfa = smem + C::kOffSFA + s * C::kSFABytes;
+          const uint32_t ssfb = smem + C::kOffSFB + s * C::kSFBBytes;
+          ptx::tmem_cp_32x128b_x4<kCtaGroup>(sfa_t, ptx::sf_chunk_desc(ssfa));
+#pragma unroll
+          for (int h = 0; h < kTileN / 128; ++h)
+            ptx::tmem_cp_32x128b_x4<kCtaGroup>(sfb_t + 4 * h, ptx::sf_chunk_desc(ssfb + 512 * h));
+          const uint64_t a_desc = ptx::kmajor_sw128_desc(sa);
+          const uint64_t b_desc = ptx::kmajor_sw128_desc(sb);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            // Advance 32 bytes (one K=32 slice) inside the 128-byte swizzled rows.
+            ptx::mma_mxf8f6f4<kCtaGroup>(d_t, a_desc + 2 * j, b_desc + 2 * j,
+                                         ptx::with_scale_id(C::kIdesc, j),
+                                         sfa_t | (static_cast<uint32_t>(j) << 30),
+                                         sfb_t | (static_cast<uint32_t>(j) << 30),
+                                         (kb | j) != 0 ? 1u : 0u);
+          }
+          ptx::tc_commit<kCtaGroup>(empty_bar(s));
+          if constexpr (kPair) ptx::tc_commit<kCtaGroup>(ptx::mapa(empty_bar(s), 1));
+        }
+        if (!ok) break;
+        ptx::tc_commit<kCtaGroup>(acc_full_bar(buf));
+        if constexpr (kPair) ptx::tc_commit<kCtaGroup>(ptx::mapa(acc_full_bar(buf), 1));
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const uint32_t cbuf = smem + C::kOffC + warp * kEpiBufs * C::kCBufBytes;
+    uint32_t chunk_ctr = 0;
+    int it = 0;
+    for (int t = cluster_id; t < args.num_tiles; t += num_clusters, ++it) {
+      int mt, nt;
+      tile_coords(t, args, mt, nt);
+      const int m_row = mt * (128 * kCtaGroup) + static_cast<int>(rank) * 128 + warp * 32;
+      const int n_col = nt * kTileN;
+      const int buf = it & 1;
+      if (!ptx::mbar_wait(acc_full_bar(buf), (it >> 1) & 1, status, kDevTimeoutEpilogue)) break;
+      ptx::tc_fence_after();
+      const uint32_t acc = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) +
+                           static_cast<uint32_t>(buf ? C::kAcc1Col : 0);
+      const int first = buf == 0 ? C::kFirstChunk0 : 0;
+#pragma unroll 1
+      for (int i = 0; i < C::kChunks; ++i) {
+        const int c = (first + i) % C::kChunks;
+        uint32_t v0[32], v1[32];
+        ptx::tmem_ld_32x32b_x32(acc + c * 64, v0);
+        ptx::tmem_ld_32x32b_x32(acc + c * 64 + 32, v1);
+        ptx::tmem_wait_ld();
+        const bool release = C::kOverlap ? (i == 0) : (i == C::kChunks - 1);
+        if (release) {
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (kPair) ptx::mbar_arrive_cluster(ptx::mapa(acc_empty_bar(buf), 0));
+            else ptx::mbar_arrive(acc_empty_bar(buf));
+          }
+        }
+        const uint32_t slot = chunk_ctr % kEpiBufs;
+        if (chunk_ctr >= static_cast<uint32_t>(kEpiBufs)) {
+          if (lane == 0) ptx::bulk_wait_group_read<kEpiBufs - 1>();
+          __syncwarp();
+        }
+        const uint32_t row_addr = cbuf + slot * C::kCBufBytes + lane * 128u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t* src = j < 4 ? &v0[j * 8] : &v1[(j - 4) * 8];
+          st_shared_v4(row_addr + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4),
+                       pack_bf16x2(src[0], src[1]), pack_bf16x2(src[2], src[3]),
+                       pack_bf16x2(src[4], src[5]), pack_bf16x2(src[6], src[7]));
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::tma_store_2d(&tmap_d, cbuf + slot * C::kCBufBytes, n_col + c * 64, m_row);
+          ptx::bulk_commit_group();
+        }
+        ++chunk_ctr;
+      }
+    }
+    if (lane == 0) ptx::bulk_wait_group_all();
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------ teardown
+  ptx::tc_fence_before();
+  if constexpr (kPair) ptx::cluster_sync(); else __syncthreads();
+  if (warp == 4) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc<kCtaGroup>(tmem_base, C::kTmemCols);
+  }
+}
+
+}  // namespace cutex

@@ -1,0 +1,15 @@
+"""B200 MXFP8 kernels behind the reference's kernel-module names."""
+
+from . import dense_gemm_contract
+from .dense_gemm import GemmConfig, dense_gemm, dense_gemm_v13, mxfp8_gemm_launch, query
+from .quantize import quantize_mxfp8
+
+__all__ = [
+    "GemmConfig",
+    "dense_gemm",
+    "dense_gemm_contract",
+    "dense_gemm_v13",
+    "mxfp8_gemm_launch",
+    "quantize_mxfp8",
+    "query",
+]

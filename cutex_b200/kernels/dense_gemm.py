@@ -1,0 +1,166 @@
+"""Python API of the B200 MXFP8 GEMM, over the C ABI of libcutex_mxfp8.so.
+
+* ``dense_gemm(a, b, sfa, sfb, out, stream=None, config=None)``: torch tensors.
+* ``dense_gemm_v13(a_ptr, b_ptr, sfa_ptr, sfb_ptr, c_ptr, max_active_clusters,
+  stream)``: the reference's fixed 16384^3 pointer interface
+  (``cutex/kernels/dense_gemm_v13.py:947-956``), raw device addresses.
+* ``mxfp8_gemm_launch``: the autotunable launcher (``@autotune`` search space
+  over native configurations, keyed by shape and device target) for
+  ``cutex_b200.compile``.
+* ``query(m, n, k, config)``: what a launch would do (grid, SMEM, stages).
+
+Operands: ``a`` [M, K] and ``b`` [N, K] E4M3 (``torch.float8_e4m3fn`` or
+``uint8``), K-major and contiguous; ``sfa``/``sfb`` flat 128x4-swizzled E8M0
+buffers (``torch.float8_e8m0fnu`` or ``uint8``) of at least
+``scale_buffer_bytes(rows, K)`` bytes; ``out`` [M, N] bf16 with unit column
+stride and a row stride that is a multiple of 8 elements.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import asdict, dataclass
+from typing import Any
+
+from .. import _lib
+from ..autotune import Config, autotune
+from .dense_gemm_contract import scale_buffer_bytes, validate_mxfp8_gemm_shape
+
+
+@dataclass(frozen=True)
+class GemmConfig:
+    """Native configuration (``cutex_gemm_config``); 0 = library heuristic for that field."""
+
+    kernel: int = 0
+    tile_n: int = 0
+    stages: int = 0
+    raster_group: int = 0
+    raster_along_n: int = 0
+    split_k: int = 0
+    max_ctas: int = 0
+    epi_buffers: int = 0
+
+    def to_c(self) -> _lib.GemmConfigC:
+        return _lib.make_config(**asdict(self))
+
+
+def _stream_handle(stream) -> int:
+    import torch
+
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    handle = getattr(stream, "cuda_stream", None)
+    if handle is None:
+        raise TypeError("stream must be a torch.cuda.Stream, a raw cudaStream_t integer or None")
+    return int(handle)
+
+
+def _byte_view_ok(t, name: str) -> None:
+    import torch
+
+    if t.dtype not in (torch.uint8, torch.float8_e4m3fn, torch.float8_e8m0fnu, torch.int8):
+        raise TypeError(f"{name} must hold bytes (float8_e4m3fn / float8_e8m0fnu / uint8); got {t.dtype}")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+
+
+def query(m: int, n: int, k: int, config: GemmConfig | None = None) -> dict[str, Any]:
+    info = _lib.GemmInfoC()
+    cfg = (config or GemmConfig()).to_c()
+    _lib.check(_lib.load().cutex_mxfp8_query(ctypes.byref(cfg), m, n, k, ctypes.byref(info)), "cutex_mxfp8_query")
+    return {name: getattr(info, name) for name, _ in _lib.GemmInfoC._fields_}
+
+
+def dense_gemm(a, b, sfa, sfb, out, stream=None, config: GemmConfig | None = None, workspace=None):
+    """D = dequant(A, SFA) @ dequant(B, SFB)^T in BF16 (FP32 accumulate); launches asynchronously."""
+
+    import torch
+
+    for t, name in ((a, "a"), (b, "b"), (sfa, "sfa"), (sfb, "sfb")):
+        _byte_view_ok(t, name)
+    if a.dim() != 2 or b.dim() != 2 or out.dim() != 2:
+        raise ValueError("a, b and out must be 2-D")
+    m, k = a.shape
+    n, kb = b.shape
+    if kb != k:
+        raise ValueError(f"a is [{m}, {k}] but b is [{n}, {kb}]: K must match")
+    validate_mxfp8_gemm_shape(m, n, k)
+    if not (a.is_contiguous() and b.is_contiguous()):
+        raise ValueError("a and b must be contiguous K-major [rows, K]")
+    if out.dtype != torch.bfloat16 or tuple(out.shape) != (m, n) or out.stride(1) != 1:
+        raise ValueError(f"out must be a bf16 [{m}, {n}] tensor with unit column stride")
+    if sfa.numel() * sfa.element_size() < scale_buffer_bytes(m, k):
+        raise ValueError(f"sfa holds {sfa.numel()} bytes; {scale_buffer_bytes(m, k)} required")
+    if sfb.numel() * sfb.element_size() < scale_buffer_bytes(n, k):
+        raise ValueError(f"sfb holds {sfb.numel()} bytes; {scale_buffer_bytes(n, k)} required")
+    cfg = (config or GemmConfig()).to_c()
+    ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
+    status = _lib.load().cutex_mxfp8_gemm(
+        a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), out.data_ptr(),
+        m, n, k, out.stride(0), ctypes.byref(cfg), ws_ptr or None, ws_bytes, _stream_handle(stream),
+    )
+    _lib.check(status, "cutex_mxfp8_gemm")
+    return out
+
+
+def dense_gemm_v13(a_ptr: int, b_ptr: int, sfa_ptr: int, sfb_ptr: int, c_ptr: int,
+                   max_active_clusters: int = 0, stream=None) -> None:
+    """The reference's fixed M=N=K=16384 five-pointer launch, on the 2-CTA kernel."""
+
+    status = _lib.load().cutex_dense_gemm_v13(
+        a_ptr, b_ptr, sfa_ptr, sfb_ptr, c_ptr, int(max_active_clusters), _stream_handle(stream)
+    )
+    _lib.check(status, "cutex_dense_gemm_v13")
+
+
+def device_target() -> str:
+    """Autotune-cache key field: GPU name, compute capability, SM count and library build."""
+
+    import torch
+
+    props = torch.cuda.get_device_properties(torch.cuda.current_device())
+    return f"{props.name}|cc{props.major}.{props.minor}|sm{props.multi_processor_count}|{_lib.version()}"
+
+
+# Search space: kernel family x tile x ring depth x raster order/group.
+GEMM_CONFIGS = (
+    [
+        Config({"kernel": 2, "tile_n": 256, "stages": s, "epi_buffers": e, "raster_group": g, "raster_along_n": r},
+               name=f"2cta_n256_s{s}_e{e}_g{g}_{'n' if r else 'm'}")
+        for s, e in ((6, 1), (5, 2), (4, 2))
+        for g in (4, 8, 16)
+        for r in (0, 1)
+    ]
+    + [
+        Config({"kernel": 1, "tile_n": 256, "stages": s, "epi_buffers": e, "raster_group": 8, "raster_along_n": 0},
+               name=f"1cta_n256_s{s}_e{e}")
+        for s, e in ((4, 1), (3, 2))
+    ]
+    + [
+        Config({"kernel": 1, "tile_n": 128, "stages": s, "epi_buffers": e, "raster_group": 8, "raster_along_n": 0},
+               name=f"1cta_n128_s{s}_e{e}")
+        for s, e in ((6, 1), (5, 2))
+    ]
+)
+
+
+@autotune(configs=GEMM_CONFIGS, key=["m", "n", "k", "target"], warmup=3, rep=10)
+def mxfp8_gemm_launch(a, b, sfa, sfb, out, m, n, k, target, stream=None, *, kernel=0, tile_n=0,
+                      stages=0, raster_group=0, raster_along_n=0, split_k=0, max_ctas=0, epi_buffers=0):
+    """Autotunable launcher: ``cutex_b200.compile(mxfp8_gemm_launch, a, b, sfa, sfb, out, m, n, k, target)``."""
+
+    cfg = GemmConfig(kernel, tile_n, stages, raster_group, raster_along_n, split_k, max_ctas, epi_buffers)
+    return dense_gemm(a, b, sfa, sfb, out, stream=stream, config=cfg)
+
+
+__all__ = [
+    "GEMM_CONFIGS",
+    "GemmConfig",
+    "dense_gemm",
+    "dense_gemm_v13",
+    "device_target",
+    "mxfp8_gemm_launch",
+    "query",
+]

@@ -1,0 +1,160 @@
+/*
+ * cutex-b200: MXFP8 block-scaled dense GEMM for NVIDIA B200 (sm_100a).
+ *
+ * C ABI of libcutex_mxfp8.so. Plain pointers and sizes only; every entry
+ * point returns a cutex_status code and never throws. Launches are
+ * asynchronous on the caller's stream; the caller allocates and owns every
+ * buffer, including the output. The GEMM entry points never allocate device
+ * memory and never synchronise.
+ *
+ * Contract (the reference's fixed Fprop contract, generalised in shape):
+ *   D[M,N] (bf16, row-major, row stride ldd elements)
+ *     = dequant(A[M,K] e4m3, SFA) . dequant(B[N,K] e4m3, SFB)^T
+ *   A and B are K-major (row-major [rows, K]); one E8M0 scale per 1x32
+ *   K-block; FP32 accumulation; BF16 output with round-to-nearest-even.
+ *
+ * Scale-factor layout (SM100 128x4 swizzle): the scale of row r and K-block
+ * c (= k/32) of an operand with K columns lives at byte
+ *     ((r/128)*(K/128) + c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4
+ * so SFA holds ceil(M/128)*128*K/32 bytes and SFB ceil(N/128)*128*K/32.
+ * Rows past M (resp. N) in the last 128-row block are padding.
+ */
+#ifndef CUTEX_MXFP8_H_
+#define CUTEX_MXFP8_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CUTEX_API __attribute__((visibility("default")))
+#else
+#define CUTEX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque stream handle; binary-compatible with cudaStream_t / CUstream. */
+typedef struct CUstream_st* cutex_stream_t;
+
+typedef enum cutex_status {
+  CUTEX_OK = 0,
+  CUTEX_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad config field */
+  CUTEX_ERR_SHAPE = 2,            /* M, N or K outside the supported range */
+  CUTEX_ERR_ALIGN = 3,            /* pointer, stride or K alignment rule violated */
+  CUTEX_ERR_UNSUPPORTED_DEVICE = 4, /* current device is not compute capability 10.0 */
+  CUTEX_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed */
+  CUTEX_ERR_TIMEOUT = 6,          /* a device-side bounded wait expired */
+  CUTEX_ERR_WORKSPACE = 7         /* workspace missing or smaller than required */
+} cutex_status;
+
+/* Kernel families. */
+enum {
+  CUTEX_KERNEL_AUTO = 0,
+  CUTEX_KERNEL_1CTA = 1,   /* persistent, 128 x tile_n per CTA, cta_group::1 MMA */
+  CUTEX_KERNEL_2CTA = 2,   /* persistent, 256 x tile_n per CTA pair, cta_group::2 MMA */
+  CUTEX_KERNEL_SKINNY = 3  /* M <= 128: swap-AB, split-K over all SMs (needs workspace) */
+};
+
+/*
+ * Tunables searched by the autotuner. Zero in any field selects the built-in
+ * heuristic for that field.
+ */
+typedef struct cutex_gemm_config {
+  int32_t kernel;         /* CUTEX_KERNEL_* */
+  int32_t tile_n;         /* 128 or 256 output columns per MMA tile */
+  int32_t stages;         /* shared-memory ring depth */
+  int32_t raster_group;   /* output tiles per rasterisation group (>= 1) */
+  int32_t raster_along_n; /* 0: walk M inside a group, 1: walk N inside a group */
+  int32_t split_k;        /* skinny kernel: K splits (0 = auto) */
+  int32_t max_ctas;       /* cap on persistent CTAs (0 = one per SM) */
+  int32_t epi_buffers;    /* epilogue staging buffers per warp (1 or 2) */
+  int32_t reserved[8];    /* must be zero */
+} cutex_gemm_config;
+
+/* What a launch with this configuration would do (filled by cutex_mxfp8_query). */
+typedef struct cutex_gemm_info {
+  int32_t kernel;
+  int32_t tile_m;          /* output rows per tile (per CTA pair for the 2-CTA kernel) */
+  int32_t tile_n;
+  int32_t tile_k;
+  int32_t stages;
+  int32_t cluster_size;
+  int32_t grid_ctas;
+  int32_t smem_bytes;
+  int32_t num_tiles;
+  int32_t split_k;
+  int32_t epi_buffers;
+  int32_t raster_group;
+  int64_t workspace_bytes; /* device workspace the GEMM call needs (0 for most shapes) */
+} cutex_gemm_info;
+
+/*
+ * MXFP8 GEMM, general shape.
+ * Replaces the reference's `@cute.jit dense_gemm_vN(a_ptr, b_ptr, sfa_ptr,
+ * sfb_ptr, c_ptr[, max_active_clusters], stream)` launch
+ * (cutex/kernels/dense_gemm_v13.py:947-956, dense_gemm_v1.py:89-97) with the
+ * shape, output stride and tile configuration as runtime arguments.
+ *   a, b, d: 16-byte aligned. sfa, sfb: 16-byte aligned.
+ *   K % 128 == 0, K >= 128; N % 16 == 0; ldd >= N and ldd % 8 == 0; M >= 1.
+ *   workspace: device buffer of at least cutex_mxfp8_query(...)->workspace_bytes
+ *   (may be NULL when that is 0). Contents need not be initialised; the call
+ *   leaves it all-zero again on return of the kernel.
+ */
+CUTEX_API int cutex_mxfp8_gemm(const void* a, const void* b, const void* sfa, const void* sfb, void* d,
+                     int64_t M, int64_t N, int64_t K, int64_t ldd,
+                     const cutex_gemm_config* cfg, void* workspace, int64_t workspace_bytes,
+                     cutex_stream_t stream);
+
+/*
+ * Resolve a configuration for a shape without launching anything.
+ * Replaces the host-side resource accounting of dense_gemm_v13
+ * (cutex/kernels/dense_gemm_v13.py:1095-1239: SMEM layouts, tma_bytes, grid).
+ */
+CUTEX_API int cutex_mxfp8_query(const cutex_gemm_config* cfg, int64_t M, int64_t N, int64_t K,
+                      cutex_gemm_info* info);
+
+/*
+ * The reference's fixed-shape entry: M = N = K = 16384, D row stride 16384,
+ * 2-CTA persistent kernel with at most `max_active_clusters` CTA pairs
+ * (<= 0: as many as fit). Mirrors `dense_gemm_v13(a_ptr, b_ptr, sfa_ptr,
+ * sfb_ptr, c_ptr, max_active_clusters, stream)`
+ * (cutex/kernels/dense_gemm_v13.py:947-956).
+ */
+CUTEX_API int cutex_dense_gemm_v13(const void* a, const void* b, const void* sfa, const void* sfb, void* c,
+                         int32_t max_active_clusters, cutex_stream_t stream);
+
+/*
+ * MXFP8 quantiser (OCP MX, E4M3 elements, E8M0 scales): for each 1x32 block
+ * of x[rows, K] (row stride ldx elements) the scale exponent is
+ * floor(log2(amax)) - 8 clamped to [-127, 127] (all-zero block -> 0x00),
+ * elements are x / 2^e rounded to nearest-even and saturated to +-448.
+ * Writes q[rows, K] (row stride K bytes) and scales in the 128x4 swizzled
+ * layout (ceil(rows/128)*128*K/32 bytes; padding rows are written as 0x00).
+ * x_dtype: 0 = float32, 1 = bfloat16. K % 128 == 0.
+ * Replaces Transformer Engine's MXFP8Quantizer(rowwise=True,
+ * optimize_for_gemm=True) call in the reference runner
+ * (modal_dense_gemm.py:358-373).
+ */
+CUTEX_API int cutex_mxfp8_quantize(const void* x, int32_t x_dtype, int64_t rows, int64_t K, int64_t ldx,
+                         void* q, void* sf, cutex_stream_t stream);
+
+/* Human-readable text for a cutex_status value (static storage). */
+CUTEX_API const char* cutex_status_string(int status);
+
+/*
+ * Synchronise `stream`, return the first device-side error recorded by a
+ * kernel of this library on the current device since the last call
+ * (CUTEX_OK or CUTEX_ERR_TIMEOUT), and clear it.
+ */
+CUTEX_API int cutex_last_device_status(cutex_stream_t stream);
+
+/* Number of SMs and the library's build identifier (for autotune cache keys). */
+CUTEX_API int cutex_device_sm_count(int32_t* sm_count);
+CUTEX_API const char* cutex_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUTEX_MXFP8_H_ */

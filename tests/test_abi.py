@@ -1,0 +1,111 @@
+"""The C-ABI library loads, exports every declared entry point, and validates arguments (no GPU needed)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from cutex_b200 import _lib
+from cutex_b200.kernels import dense_gemm_contract as C
+
+HEADERS = sorted((Path(__file__).resolve().parents[1] / "include").glob("*.h"))
+
+
+def declared_functions():
+    names = []
+    for h in HEADERS:
+        text = h.read_text()
+        names += re.findall(r"CUTEX_API\s+[\w\s\*]+?\b(cutex_\w+)\s*\(", text)
+    return names
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    assert "cutex_mxfp8_gemm" in names and "cutex_mxfp8_query" in names
+    assert len(names) == len(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert set(declared_functions()) == set(_lib.SIGNATURES)
+
+
+def test_struct_layouts_match_header():
+    assert ctypes.sizeof(_lib.GemmConfigC) == 16 * 4
+    assert ctypes.sizeof(_lib.GemmInfoC) == 12 * 4 + 8
+
+
+def test_status_strings():
+    for code in range(8):
+        assert _lib.status_string(code).startswith("CUTEX_")
+    assert "UNKNOWN" in _lib.status_string(99)
+    assert _lib.version().startswith("cutex-b200")
+
+
+FAKE = 1 << 20  # a 16-byte aligned non-null address; never dereferenced by argument validation
+
+
+def gemm(a=FAKE, b=FAKE, sfa=FAKE, sfb=FAKE, d=FAKE, M=256, N=256, K=256, ldd=256, cfg=None, ws=None, wsb=0):
+    c = cfg if cfg is not None else _lib.GemmConfigC()
+    return _lib.load().cutex_mxfp8_gemm(a, b, sfa, sfb, d, M, N, K, ldd, ctypes.byref(c), ws, wsb, None)
+
+
+@pytest.mark.parametrize(
+    "kwargs,status",
+    [
+        ({"a": None}, _lib.CUTEX_ERR_INVALID_ARGUMENT),
+        ({"d": None}, _lib.CUTEX_ERR_INVALID_ARGUMENT),
+        ({"M": 0}, _lib.CUTEX_ERR_SHAPE),
+        ({"K": -128}, _lib.CUTEX_ERR_SHAPE),
+        ({"K": 200}, _lib.CUTEX_ERR_ALIGN),
+        ({"N": 24, "ldd": 24}, _lib.CUTEX_ERR_ALIGN),
+        ({"ldd": 255}, _lib.CUTEX_ERR_ALIGN),
+        ({"ldd": 128}, _lib.CUTEX_ERR_ALIGN),
+        ({"a": FAKE + 8}, _lib.CUTEX_ERR_ALIGN),
+        ({"sfb": FAKE + 4}, _lib.CUTEX_ERR_ALIGN),
+        ({"wsb": -1}, _lib.CUTEX_ERR_INVALID_ARGUMENT),
+    ],
+)
+def test_gemm_argument_validation(kwargs, status):
+    assert gemm(**kwargs) == status
+
+
+def test_query_resolves_plans_without_launching():
+    info = _lib.GemmInfoC()
+    cfg = _lib.GemmConfigC()
+    lib = _lib.load()
+    assert lib.cutex_mxfp8_query(ctypes.byref(cfg), C.M, C.N, C.K, ctypes.byref(info)) == 0
+    assert info.kernel == _lib.KERNEL_2CTA and info.tile_m == 256 and info.tile_n == 256
+    assert info.cluster_size == 2 and info.num_tiles == 64 * 64
+    assert info.smem_bytes <= 232448 and info.grid_ctas % 2 == 0
+    cfg = _lib.make_config(kernel=1, tile_n=128, stages=5)
+    assert lib.cutex_mxfp8_query(ctypes.byref(cfg), 300, 272, 384, ctypes.byref(info)) == 0
+    assert (info.tile_m, info.tile_n, info.stages, info.num_tiles) == (128, 128, 5, 3 * 3)
+    bad = _lib.make_config(tile_n=96)
+    assert lib.cutex_mxfp8_query(ctypes.byref(bad), 256, 256, 256, ctypes.byref(info)) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    bad = _lib.GemmConfigC()
+    bad.reserved[3] = 1
+    assert lib.cutex_mxfp8_query(ctypes.byref(bad), 256, 256, 256, ctypes.byref(info)) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    bad = _lib.make_config(stages=9)
+    assert lib.cutex_mxfp8_query(ctypes.byref(bad), 256, 256, 256, ctypes.byref(info)) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+
+
+def test_quantize_argument_validation():
+    lib = _lib.load()
+    assert lib.cutex_mxfp8_quantize(None, 0, 4, 128, 128, FAKE, FAKE, None) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    assert lib.cutex_mxfp8_quantize(FAKE, 2, 4, 128, 128, FAKE, FAKE, None) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    assert lib.cutex_mxfp8_quantize(FAKE, 0, 4, 96, 96, FAKE, FAKE, None) == _lib.CUTEX_ERR_ALIGN
+    assert lib.cutex_mxfp8_quantize(FAKE, 0, 0, 128, 128, FAKE, FAKE, None) == _lib.CUTEX_ERR_SHAPE
+
+
+def test_python_wrapper_rejects_with_value_errors():
+    from cutex_b200.kernels.dense_gemm import GemmConfig, query
+
+    with pytest.raises(ValueError):
+        query(256, 256, 200)
+    with pytest.raises(ValueError):
+        query(256, 256, 256, GemmConfig(tile_n=64))
+    assert query(16, 28672, 8192)["tile_m"] == 128
