@@ -37,7 +37,8 @@ class GemmConfigC(ctypes.Structure):
         ("split_k", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32),
         ("epi_buffers", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 8),
+        ("sf_buffers", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 7),
     ]
 
 
@@ -55,6 +56,8 @@ class GemmInfoC(ctypes.Structure):
         ("split_k", ctypes.c_int32),
         ("epi_buffers", ctypes.c_int32),
         ("raster_group", ctypes.c_int32),
+        ("sf_buffers", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
         ("workspace_bytes", ctypes.c_int64),
     ]
 

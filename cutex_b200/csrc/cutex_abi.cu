@@ -116,40 +116,44 @@ using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CU
                           GemmArgs);
 
 struct Variant {
-  int cta_group, tile_n, stages, epi_bufs, smem_bytes;
+  int cta_group, tile_n, stages, epi_bufs, sf_bufs, smem_bytes;
   const void* fn;
   bool attr_set[kMaxDevices];
   int max_clusters[kMaxDevices];
 };
 
-template <int CG, int BN, int S, int E>
+template <int CG, int BN, int S, int E, int F>
 Variant make_variant() {
   Variant v{};
   v.cta_group = CG;
   v.tile_n = BN;
   v.stages = S;
   v.epi_bufs = E;
-  v.smem_bytes = GemmCfg<CG, BN, S, E>::kSmemBytes;
-  v.fn = reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E>);
+  v.sf_bufs = F;
+  v.smem_bytes = GemmCfg<CG, BN, S, E, F>::kSmemBytes;
+  v.fn = reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F>);
   return v;
 }
 
+// Instantiated kernels: (cta group, tile_n, stages, epilogue buffers, SF buffers).
 Variant g_variants[] = {
-    make_variant<1, 128, 4, 2>(), make_variant<1, 128, 5, 2>(), make_variant<1, 128, 6, 1>(),
-    make_variant<1, 256, 3, 2>(), make_variant<1, 256, 4, 1>(), make_variant<2, 256, 4, 2>(),
-    make_variant<2, 256, 5, 2>(), make_variant<2, 256, 6, 1>(),
+    make_variant<1, 128, 4, 2, 2>(), make_variant<1, 128, 5, 2, 2>(), make_variant<1, 128, 6, 1, 2>(),
+    make_variant<1, 128, 6, 1, 1>(), make_variant<1, 256, 3, 2, 2>(), make_variant<1, 256, 4, 1, 2>(),
+    make_variant<1, 256, 4, 1, 1>(), make_variant<2, 256, 4, 2, 2>(), make_variant<2, 256, 5, 2, 2>(),
+    make_variant<2, 256, 6, 1, 2>(), make_variant<2, 256, 6, 1, 1>(), make_variant<2, 256, 6, 1, 4>(),
+    make_variant<2, 256, 5, 2, 1>(), make_variant<2, 256, 5, 2, 4>(),
 };
 
-Variant* find_variant(int cg, int bn, int stages, int epi) {
+Variant* find_variant(int cg, int bn, int stages, int epi, int sfb) {
   Variant* best = nullptr;
   for (auto& v : g_variants) {
     if (v.cta_group != cg || v.tile_n != bn) continue;
     if (stages != 0 && v.stages != stages) continue;
     if (epi != 0 && v.epi_bufs != epi) continue;
-    // Default: deepest ring, then the most epilogue buffers.
-    if (best == nullptr || v.stages > best->stages ||
-        (v.stages == best->stages && v.epi_bufs > best->epi_bufs))
-      best = &v;
+    if (sfb != 0 && v.sf_bufs != sfb) continue;
+    // Default: deepest ring, then two SF buffers, then the most epilogue buffers.
+    auto rank = [](const Variant& x) { return x.stages * 100 + (x.sf_bufs == 2 ? 10 : 0) + x.epi_bufs; };
+    if (best == nullptr || rank(v) > rank(*best)) best = &v;
   }
   return best;
 }
@@ -186,6 +190,7 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   }
   if (cfg.kernel < 0 || cfg.kernel > CUTEX_KERNEL_SKINNY || cfg.stages < 0 || cfg.raster_group < 0 ||
       cfg.max_ctas < 0 || cfg.split_k < 0 || cfg.epi_buffers < 0 || cfg.epi_buffers > 2 ||
+      cfg.sf_buffers < 0 || cfg.sf_buffers > 4 ||
       (cfg.raster_along_n != 0 && cfg.raster_along_n != 1))
     return CUTEX_ERR_INVALID_ARGUMENT;
   if (cfg.tile_n != 0 && cfg.tile_n != 128 && cfg.tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
@@ -200,7 +205,7 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
     tile_n = (N % 256 == 0 && M > 128) ? 256 : 128;
   }
   const int cg = kernel == CUTEX_KERNEL_2CTA ? 2 : 1;
-  Variant* v = find_variant(cg, tile_n, cfg.stages, cfg.epi_buffers);
+  Variant* v = find_variant(cg, tile_n, cfg.stages, cfg.epi_buffers, cfg.sf_buffers);
   if (v == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
   plan->variant = v;
   plan->kernel = kernel;
@@ -310,6 +315,7 @@ extern "C" int cutex_mxfp8_query(const cutex_gemm_config* cfg, int64_t M, int64_
   info->num_tiles = plan.num_tiles;
   info->split_k = 1;
   info->epi_buffers = plan.variant->epi_bufs;
+  info->sf_buffers = plan.variant->sf_bufs;
   info->raster_group = plan.raster_group;
   info->workspace_bytes = 0;
   return CUTEX_OK;

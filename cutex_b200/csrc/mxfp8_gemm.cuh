@@ -16,12 +16,13 @@
 //              kStages-deep ring guarded by full/empty mbarriers.
 //
 // TMEM plan (512 columns, 32-bit): two accumulator buffers alternate by tile.
-// When two full buffers plus the 16 scale-factor columns do not fit (tile_n =
-// 256), buffer 1 starts at column 240 and overlaps the last 16 columns of
+// When two full buffers plus the scale-factor columns do not fit (tile_n =
+// 256), buffer 1 starts at column 512 - 256 - 16*kSFBufs and overlaps the end of
 // buffer 0; the epilogue reads the overlapping 64-column chunk first and then
 // releases the accumulator, so the next tile's MMAs start while the rest of
 // the tile is still being stored. Scale factors: SFA 4 columns (128 rows),
-// SFB 4 columns per 128 rows of N, byte k of a column = K-block k of a stage.
+// SFB 4 columns per 128 rows of N, byte k of a column = K-block k of a stage,
+// in kSFBufs rotating 16-column buffers at the top of TMEM.
 //
 // K-stage: 128 K values. A stage holds the A tile (128 x 128 B), this CTA's B
 // rows (kTileN/kCtaGroup x 128 B), the 512-byte SFA chunk and the full SFB
@@ -60,7 +61,7 @@ constexpr int kSmemLimit = 232448;  // max dynamic shared memory per block on sm
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs>
+template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs, int kSFBufs>
 struct GemmCfg {
   static constexpr int kThreads = 192;
   static constexpr int kTileM = 128;  // rows per CTA
@@ -87,7 +88,11 @@ struct GemmCfg {
   static constexpr int kTmemCols = 512;
   static constexpr int kSFACols = 4;
   static constexpr int kSFBCols = (kTileN / 128) * 4;
-  static constexpr int kSFReserved = 16;
+  // Scale factors rotate through kSFBufs 16-column buffers (one per K-stage in
+  // flight), so the SMEM->TMEM copy of stage k+1 never waits for the MMAs of
+  // stage k to finish reading the previous scales.
+  static constexpr int kSFBufCols = 16;
+  static constexpr int kSFReserved = kSFBufCols * kSFBufs;
   static constexpr bool kOverlap = 2 * kTileN + kSFReserved > kTmemCols;
   static constexpr int kAcc1Col = kOverlap ? (kTmemCols - kSFReserved - kTileN) : kTileN;
   static constexpr int kSFACol = kOverlap ? (kTmemCols - kSFReserved) : 2 * kTileN;
@@ -100,8 +105,9 @@ struct GemmCfg {
   static_assert(kCtaGroup == 1 || kCtaGroup == 2, "cta group");
   static_assert(kTileN == 128 || kTileN == 256, "tile_n");
   static_assert(kCtaGroup == 1 || kTileN == 256, "the CTA-pair kernel uses tile_n = 256");
-  static_assert(kSFACols + kSFBCols <= kSFReserved, "scale-factor columns");
-  static_assert(kSFBCol + kSFBCols <= kTmemCols, "TMEM plan");
+  static_assert(kSFACols + kSFBCols <= kSFBufCols, "scale-factor columns");
+  static_assert(kSFBufs == 1 || kSFBufs == 2 || kSFBufs == 4, "scale-factor buffers");
+  static_assert(kSFACol + kSFReserved <= kTmemCols, "TMEM plan");
   static_assert(!kOverlap || (kTileN - kAcc1Col) <= 64 - (kAcc1Col % 64),
                 "overlap must sit inside one epilogue chunk");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
@@ -148,14 +154,14 @@ __device__ __forceinline__ void settle_inflight_copies() {
   while (ptx::globaltimer() - t0 < 50000ull) __nanosleep(1000);
 }
 
-template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs>
+template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs, int kSFBufs>
 __global__ void __launch_bounds__(192, 1)
     mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_sfa,
                       const __grid_constant__ CUtensorMap tmap_sfb,
                       const __grid_constant__ CUtensorMap tmap_d, const GemmArgs args) {
-  using C = GemmCfg<kCtaGroup, kTileN, kStages, kEpiBufs>;
+  using C = GemmCfg<kCtaGroup, kTileN, kStages, kEpiBufs, kSFBufs>;
   constexpr bool kPair = kCtaGroup == 2;
 
   extern __shared__ uint8_t smem_raw[];
@@ -258,8 +264,6 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t kit = 0;
       bool ok = true;
       int it = 0;
-      const uint32_t sfa_t = tmem_base + C::kSFACol;
-      const uint32_t sfb_t = tmem_base + C::kSFBCol;
       for (int t = cluster_id; ok && t < args.num_tiles; t += num_clusters, ++it) {
         const int buf = it & 1;
         if constexpr (C::kOverlap) {
@@ -285,6 +289,9 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t sb = smem + C::kOffB + s * C::kBBytes;
           const uint32_t ssfa = smem + C::kOffSFA + s * C::kSFABytes;
           const uint32_t ssfb = smem + C::kOffSFB + s * C::kSFBBytes;
+          const uint32_t sf_off = static_cast<uint32_t>(kit % kSFBufs) * C::kSFBufCols;
+          const uint32_t sfa_t = tmem_base + C::kSFACol + sf_off;
+          const uint32_t sfb_t = tmem_base + C::kSFBCol + sf_off;
           ptx::tmem_cp_32x128b_x4<kCtaGroup>(sfa_t, ptx::sf_chunk_desc(ssfa));
 #pragma unroll
           for (int h = 0; h < kTileN / 128; ++h)

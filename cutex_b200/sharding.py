@@ -57,9 +57,9 @@ def allgather_columns(d_local, world: int, group=None):
     import torch.distributed as dist
 
     m, n_local = d_local.shape
-    gathered = torch.empty((world, m, n_local), dtype=d_local.dtype, device=d_local.device)
+    gathered = torch.empty((world * m, n_local), dtype=d_local.dtype, device=d_local.device)
     dist.all_gather_into_tensor(gathered, d_local.contiguous(), group=group)
-    return gathered.permute(1, 0, 2).reshape(m, world * n_local)
+    return gathered.view(world, m, n_local).permute(1, 0, 2).reshape(m, world * n_local)
 
 
 __all__ = ["SHARD_ALIGN", "Shard", "allgather_columns", "scale_rows_slice", "shard_bounds"]

@@ -69,7 +69,8 @@ typedef struct cutex_gemm_config {
   int32_t split_k;        /* skinny kernel: K splits (0 = auto) */
   int32_t max_ctas;       /* cap on persistent CTAs (0 = one per SM) */
   int32_t epi_buffers;    /* epilogue staging buffers per warp (1 or 2) */
-  int32_t reserved[8];    /* must be zero */
+  int32_t sf_buffers;     /* rotating scale-factor TMEM buffers (1, 2 or 4) */
+  int32_t reserved[7];    /* must be zero */
 } cutex_gemm_config;
 
 /* What a launch with this configuration would do (filled by cutex_mxfp8_query). */
@@ -86,6 +87,8 @@ typedef struct cutex_gemm_info {
   int32_t split_k;
   int32_t epi_buffers;
   int32_t raster_group;
+  int32_t sf_buffers;
+  int32_t reserved0;
   int64_t workspace_bytes; /* device workspace the GEMM call needs (0 for most shapes) */
 } cutex_gemm_info;
 

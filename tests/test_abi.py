@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_struct_layouts_match_header():
     assert ctypes.sizeof(_lib.GemmConfigC) == 16 * 4
-    assert ctypes.sizeof(_lib.GemmInfoC) == 12 * 4 + 8
+    assert ctypes.sizeof(_lib.GemmInfoC) == 14 * 4 + 8
 
 
 def test_status_strings():

@@ -22,11 +22,16 @@ VARIANTS = [
     GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1),
     GemmConfig(kernel=2, tile_n=256, stages=5, epi_buffers=2),
     GemmConfig(kernel=2, tile_n=256, stages=4, epi_buffers=2),
+    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1, sf_buffers=1),
+    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1, sf_buffers=4),
+    GemmConfig(kernel=2, tile_n=256, stages=5, epi_buffers=2, sf_buffers=4),
+    GemmConfig(kernel=1, tile_n=256, stages=4, epi_buffers=1, sf_buffers=1),
+    GemmConfig(kernel=1, tile_n=128, stages=6, epi_buffers=1, sf_buffers=1),
 ]
 
 
 def _id(cfg):
-    return f"k{cfg.kernel}_n{cfg.tile_n}_s{cfg.stages}_e{cfg.epi_buffers}"
+    return f"k{cfg.kernel}_n{cfg.tile_n}_s{cfg.stages}_e{cfg.epi_buffers}_f{cfg.sf_buffers}"
 
 
 def _assert_ok(report):
