@@ -118,11 +118,13 @@ using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CU
 struct Variant {
   int cta_group, tile_n, stages, epi_bufs, sf_bufs, smem_bytes;
   const void* fn;
+  const void* fn_trace;  // instrumented twin (cutex_mxfp8_gemm_trace), or null
+  bool attr_set_trace[kMaxDevices];
   bool attr_set[kMaxDevices];
   int max_clusters[kMaxDevices];
 };
 
-template <int CG, int BN, int S, int E, int F>
+template <int CG, int BN, int S, int E, int F, bool T = false>
 Variant make_variant() {
   Variant v{};
   v.cta_group = CG;
@@ -132,6 +134,7 @@ Variant make_variant() {
   v.sf_bufs = F;
   v.smem_bytes = GemmCfg<CG, BN, S, E, F>::kSmemBytes;
   v.fn = reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F>);
+  v.fn_trace = T ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, true>) : nullptr;
   return v;
 }
 
@@ -139,9 +142,9 @@ Variant make_variant() {
 Variant g_variants[] = {
     make_variant<1, 128, 4, 2, 2>(), make_variant<1, 128, 5, 2, 2>(), make_variant<1, 128, 6, 1, 2>(),
     make_variant<1, 128, 6, 1, 1>(), make_variant<1, 256, 3, 2, 2>(), make_variant<1, 256, 4, 1, 2>(),
-    make_variant<1, 256, 4, 1, 1>(), make_variant<2, 256, 4, 2, 2>(), make_variant<2, 256, 5, 2, 2>(),
-    make_variant<2, 256, 6, 1, 2>(), make_variant<2, 256, 6, 1, 1>(), make_variant<2, 256, 6, 1, 4>(),
-    make_variant<2, 256, 5, 2, 1>(), make_variant<2, 256, 5, 2, 4>(),
+    make_variant<1, 256, 4, 1, 1, true>(), make_variant<2, 256, 4, 2, 2>(), make_variant<2, 256, 5, 2, 2>(),
+    make_variant<2, 256, 6, 1, 2>(), make_variant<2, 256, 6, 1, 1, true>(), make_variant<2, 256, 6, 1, 4>(),
+    make_variant<2, 256, 5, 2, 1, true>(), make_variant<2, 256, 5, 2, 4>(),
 };
 
 Variant* find_variant(int cg, int bn, int stages, int epi, int sfb) {
@@ -228,8 +231,11 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const void* sfa,
                 const void* sfb, void* d, int64_t M, int64_t N, int64_t K, int64_t ldd,
-                cudaStream_t stream) {
+                cudaStream_t stream, unsigned long long* trace = nullptr, int trace_cap = 0) {
   Variant* v = plan.variant;
+  const bool traced = trace != nullptr;
+  if (traced && v->fn_trace == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  const void* fn = traced ? v->fn_trace : v->fn;
   const int cg = v->cta_group;
   CUtensorMap ta, tb, tsa, tsb, td;
   if (!encode_operand(&ta, a, M, K, 128) || !encode_operand(&tb, b, N, K, v->tile_n / cg) ||
@@ -238,11 +244,12 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
     return CUTEX_ERR_CUDA;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (!v->attr_set[dev]) {
-      if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               v->smem_bytes) != cudaSuccess)
+    bool& set = traced ? v->attr_set_trace[dev] : v->attr_set[dev];
+    if (!set) {
+      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v->smem_bytes) !=
+          cudaSuccess)
         return CUTEX_ERR_CUDA;
-      v->attr_set[dev] = true;
+      set = true;
     }
   }
   GemmArgs args{};
@@ -252,6 +259,8 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
   args.num_k_blocks = static_cast<int>(K / 128);
   args.raster_group = plan.raster_group;
   args.raster_along_n = plan.raster_along_n;
+  args.trace = trace;
+  args.trace_cap = trace_cap;
 
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(static_cast<unsigned>(plan.grid_ctas), 1, 1);
@@ -274,7 +283,7 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
       max_clusters = v->max_clusters[dev];
     }
     if (max_clusters == 0) {
-      if (cudaOccupancyMaxActiveClusters(&max_clusters, v->fn, &lc) != cudaSuccess ||
+      if (cudaOccupancyMaxActiveClusters(&max_clusters, fn, &lc) != cudaSuccess ||
           max_clusters < 1)
         return CUTEX_ERR_CUDA;
       std::lock_guard<std::mutex> lock(g_mutex);
@@ -283,7 +292,7 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
     if (plan.grid_ctas > 2 * max_clusters) lc.gridDim.x = static_cast<unsigned>(2 * max_clusters);
   }
   void* params[] = {&ta, &tb, &tsa, &tsb, &td, &args};
-  if (cudaLaunchKernelExC(&lc, v->fn, params) != cudaSuccess) return CUTEX_ERR_CUDA;
+  if (cudaLaunchKernelExC(&lc, fn, params) != cudaSuccess) return CUTEX_ERR_CUDA;
   return CUTEX_OK;
 }
 
@@ -344,6 +353,32 @@ extern "C" int cutex_mxfp8_gemm(const void* a, const void* b, const void* sfa, c
   if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
   return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd,
                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cutex_mxfp8_gemm_trace(const void* a, const void* b, const void* sfa,
+                                      const void* sfb, void* d, int64_t M, int64_t N, int64_t K,
+                                      int64_t ldd, const cutex_gemm_config* cfg,
+                                      unsigned long long* trace, int32_t trace_cap,
+                                      cutex_stream_t stream) {
+  if (a == nullptr || b == nullptr || sfa == nullptr || sfb == nullptr || d == nullptr ||
+      trace == nullptr || trace_cap < 1)
+    return CUTEX_ERR_INVALID_ARGUMENT;
+  int st = validate_shape(M, N, K);
+  if (st != CUTEX_OK) return st;
+  if (ldd < N || ldd % 8 != 0 || ldd > kMaxDim) return CUTEX_ERR_ALIGN;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(sfa) || !aligned16(sfb) || !aligned16(d) ||
+      (reinterpret_cast<uintptr_t>(trace) & 7u) != 0)
+    return CUTEX_ERR_ALIGN;
+  DeviceState* ds = nullptr;
+  st = current_device_state(&ds);
+  if (st != CUTEX_OK) return st;
+  Plan plan{};
+  st = resolve_plan(cfg, M, N, K, ds->sm_count, &plan);
+  if (st != CUTEX_OK) return st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
+  return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd,
+                     reinterpret_cast<cudaStream_t>(stream), trace, trace_cap);
 }
 
 extern "C" int cutex_dense_gemm_v13(const void* a, const void* b, const void* sfa, const void* sfb,

@@ -55,6 +55,60 @@ struct GemmArgs {
   int num_k_blocks;  // K / 128
   int raster_group;
   int raster_along_n;
+  unsigned long long* trace;  // traced builds only: event buffer (see Tracer)
+  int trace_cap;              // events per (CTA, role) region
+};
+
+// In-kernel event trace of the first CTA (pair): each role's recording thread
+// appends (globaltimer ns, event << 56 | tile << 24 | k_block) records to its own
+// region [rank * 3 + role] of `trace`; record 0 of a region holds the count.
+// Compiled only into the kTrace instantiations, never into benchmarked kernels.
+enum TraceEvent : uint32_t {
+  kEvStart = 1,
+  kEvEnd = 2,
+  kEvProdWait = 3,    // producer: wait for an empty stage
+  kEvProdGo = 4,      // producer: stage free, TMA issued next
+  kEvMmaAccWait = 5,  // MMA: wait for the accumulator (epilogue release)
+  kEvMmaAccGo = 6,
+  kEvMmaFullWait = 7,  // MMA: wait for a loaded stage
+  kEvMmaFullGo = 8,
+  kEvMmaIssued = 9,    // MMA: stage's MMAs issued and committed
+  kEvMmaTileDone = 10,
+  kEvEpiWait = 11,  // epilogue: wait for a finished accumulator
+  kEvEpiGo = 12,
+  kEvEpiRelease = 13,
+  kEvEpiTileDone = 14,
+};
+
+template <bool kOn>
+struct Tracer {
+  unsigned long long* region = nullptr;
+  int cap = 0;
+  int n = 0;
+  __device__ __forceinline__ void open(const GemmArgs& a, bool traced_cta, int region_idx) {
+    if constexpr (kOn) {
+      if (traced_cta && a.trace != nullptr) {
+        region = a.trace + static_cast<size_t>(region_idx) * (a.trace_cap + 1) * 2;
+        cap = a.trace_cap;
+      }
+    }
+  }
+  __device__ __forceinline__ void rec(uint32_t ev, int tile, int kb) {
+    if constexpr (kOn) {
+      if (region != nullptr && n < cap) {
+        region[2 * (n + 1)] = ptx::globaltimer();
+        region[2 * (n + 1) + 1] = (static_cast<unsigned long long>(ev) << 56) |
+                                  (static_cast<unsigned long long>(tile & 0xFFFFFFF) << 24) |
+                                  static_cast<unsigned long long>(kb & 0xFFFFFF);
+        ++n;
+      }
+    }
+  }
+  __device__ __forceinline__ void close() {
+    if constexpr (kOn) {
+      if (region != nullptr) region[0] = static_cast<unsigned long long>(n);
+    }
+  }
 };
 
 constexpr int kSmemLimit = 232448;  // max dynamic shared memory per block on sm_100
@@ -154,7 +208,7 @@ __device__ __forceinline__ void settle_inflight_copies() {
   while (ptx::globaltimer() - t0 < 50000ull) __nanosleep(1000);
 }
 
-template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs, int kSFBufs>
+template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs, int kSFBufs, bool kTrace = false>
 __global__ void __launch_bounds__(192, 1)
     mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -208,10 +262,13 @@ __global__ void __launch_bounds__(192, 1)
   if constexpr (kPair) ptx::cluster_sync(); else __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  Tracer<kTrace> tr;
 
   if (warp == 5) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      tr.open(args, cluster_id == 0, static_cast<int>(rank) * 3 + 0);
+      tr.rec(kEvStart, 0, 0);
       uint32_t kit = 0;
       bool ok = true;
       for (int t = cluster_id; ok && t < args.num_tiles; t += num_clusters) {
@@ -224,10 +281,12 @@ __global__ void __launch_bounds__(192, 1)
         for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
           const int s = static_cast<int>(kit % kStages);
           const uint32_t round = kit / kStages;
+          tr.rec(kEvProdWait, t, kb);
           if (!ptx::mbar_wait(empty_bar(s), (round & 1u) ^ 1u, status, kDevTimeoutProducer)) {
             ok = false;
             break;
           }
+          tr.rec(kEvProdGo, t, kb);
           if (leader) ptx::mbar_arrive_expect_tx(full_bar(s), C::kTxBytes);
           const uint32_t sa = smem + C::kOffA + s * C::kABytes;
           const uint32_t sb = smem + C::kOffB + s * C::kBBytes;
@@ -256,16 +315,21 @@ __global__ void __launch_bounds__(192, 1)
                             ((k2 / kStages) & 1u) ^ 1u, status, kDevTimeoutProducer);
       }
       if (!ok) settle_inflight_copies();
+      tr.rec(kEvEnd, 0, 0);
+      tr.close();
     }
     __syncwarp();
   } else if (warp == 4) {
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
+      tr.open(args, cluster_id == 0, 1);
+      tr.rec(kEvStart, 0, 0);
       uint32_t kit = 0;
       bool ok = true;
       int it = 0;
       for (int t = cluster_id; ok && t < args.num_tiles; t += num_clusters, ++it) {
         const int buf = it & 1;
+        tr.rec(kEvMmaAccWait, t, 0);
         if constexpr (C::kOverlap) {
           if (it >= 1)
             ok = ptx::mbar_wait<kPair>(acc_empty_bar((it - 1) & 1), ((it - 1) >> 1) & 1, status,
@@ -276,14 +340,17 @@ __global__ void __launch_bounds__(192, 1)
                                        kDevTimeoutAccEmpty);
         }
         if (!ok) break;
+        tr.rec(kEvMmaAccGo, t, 0);
         ptx::tc_fence_after();
         const uint32_t d_t = tmem_base + (buf ? C::kAcc1Col : 0);
         for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
           const int s = static_cast<int>(kit % kStages);
+          tr.rec(kEvMmaFullWait, t, kb);
           if (!ptx::mbar_wait(full_bar(s), (kit / kStages) & 1u, status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
+          tr.rec(kEvMmaFullGo, t, kb);
           ptx::tc_fence_after();
           const uint32_t sa = smem + C::kOffA + s * C::kABytes;
           const uint32_t sb = smem + C::kOffB + s * C::kBBytes;
@@ -309,11 +376,15 @@ __global__ void __launch_bounds__(192, 1)
           }
           ptx::tc_commit<kCtaGroup>(empty_bar(s));
           if constexpr (kPair) ptx::tc_commit<kCtaGroup>(ptx::mapa(empty_bar(s), 1));
+          tr.rec(kEvMmaIssued, t, kb);
         }
         if (!ok) break;
         ptx::tc_commit<kCtaGroup>(acc_full_bar(buf));
         if constexpr (kPair) ptx::tc_commit<kCtaGroup>(ptx::mapa(acc_full_bar(buf), 1));
+        tr.rec(kEvMmaTileDone, t, 0);
       }
+      tr.rec(kEvEnd, 0, 0);
+      tr.close();
     }
     __syncwarp();
   } else {
@@ -321,13 +392,17 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t cbuf = smem + C::kOffC + warp * kEpiBufs * C::kCBufBytes;
     uint32_t chunk_ctr = 0;
     int it = 0;
+    if (warp == 0 && lane == 0) tr.open(args, cluster_id == 0, static_cast<int>(rank) * 3 + 2);
+    tr.rec(kEvStart, 0, 0);
     for (int t = cluster_id; t < args.num_tiles; t += num_clusters, ++it) {
       int mt, nt;
       tile_coords(t, args, mt, nt);
       const int m_row = mt * (128 * kCtaGroup) + static_cast<int>(rank) * 128 + warp * 32;
       const int n_col = nt * kTileN;
       const int buf = it & 1;
+      tr.rec(kEvEpiWait, t, 0);
       if (!ptx::mbar_wait(acc_full_bar(buf), (it >> 1) & 1, status, kDevTimeoutEpilogue)) break;
+      tr.rec(kEvEpiGo, t, 0);
       ptx::tc_fence_after();
       const uint32_t acc = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) +
                            static_cast<uint32_t>(buf ? C::kAcc1Col : 0);
@@ -347,6 +422,7 @@ __global__ void __launch_bounds__(192, 1)
             if constexpr (kPair) ptx::mbar_arrive_cluster(ptx::mapa(acc_empty_bar(buf), 0));
             else ptx::mbar_arrive(acc_empty_bar(buf));
           }
+          tr.rec(kEvEpiRelease, t, 0);
         }
         const uint32_t slot = chunk_ctr % kEpiBufs;
         if (chunk_ctr >= static_cast<uint32_t>(kEpiBufs)) {
@@ -369,9 +445,12 @@ __global__ void __launch_bounds__(192, 1)
         }
         ++chunk_ctr;
       }
+      tr.rec(kEvEpiTileDone, t, 0);
     }
     if (lane == 0) ptx::bulk_wait_group_all();
     __syncwarp();
+    tr.rec(kEvEnd, 0, 0);
+    tr.close();
   }
 
   // ------------------------------------------------------------ teardown

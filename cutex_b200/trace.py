@@ -1,0 +1,183 @@
+"""In-kernel event tracing of the MXFP8 GEMM (replaces the reference's IKET tracing).
+
+The reference collects in-kernel ranges with the external ``run-iket`` profiler
+(``cutex/trace.py:96-175``) from one cluster selected by a predicate
+(``dense_gemm_v9.py:116-122``). Here the kernel itself has an instrumented
+twin (``cutex_mxfp8_gemm_trace``) that records ``%globaltimer`` events of the
+first CTA pair per warp role: TMA producer, MMA issuer, epilogue warp 0. This
+module runs it, decodes the records, summarises where each role waited, and
+writes a Chrome/Perfetto trace (``chrome://tracing`` / ui.perfetto.dev).
+Benchmark builds carry no instrumentation (``disabled_trace_metadata``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any
+
+from . import _lib
+
+ROLES = ("producer", "mma", "epilogue")
+EVENTS = {
+    1: "start", 2: "end", 3: "prod_wait", 4: "prod_go", 5: "mma_acc_wait", 6: "mma_acc_go",
+    7: "mma_full_wait", 8: "mma_full_go", 9: "mma_issued", 10: "mma_tile_done",
+    11: "epi_wait", 12: "epi_go", 13: "epi_release", 14: "epi_tile_done",
+}
+# (begin event, end event) -> span name
+SPANS = {
+    ("prod_wait", "prod_go"): "wait empty stage",
+    ("mma_acc_wait", "mma_acc_go"): "wait accumulator",
+    ("mma_full_wait", "mma_full_go"): "wait loaded stage",
+    ("mma_full_go", "mma_issued"): "issue MMAs",
+    ("epi_wait", "epi_go"): "wait accumulator full",
+    ("epi_go", "epi_release"): "read overlap + release",
+    ("epi_go", "epi_tile_done"): "drain tile",
+}
+
+
+class TraceError(RuntimeError):
+    """The traced launch failed or produced no events."""
+
+
+@dataclass
+class Event:
+    cta: int
+    role: str
+    t_ns: int
+    name: str
+    tile: int
+    k_block: int
+
+
+@dataclass
+class GemmTrace:
+    events: list[Event]
+    capacity: int
+    shape: tuple[int, int, int]
+    config: dict[str, Any] = field(default_factory=dict)
+
+    def role_events(self, cta: int, role: str) -> list[Event]:
+        return [e for e in self.events if e.cta == cta and e.role == role]
+
+    def spans(self, cta: int, role: str):
+        """(name, begin_ns, end_ns, tile, k_block) for every matched begin/end pair of a role."""
+
+        evs = self.role_events(cta, role)
+        out = []
+        for (b, e), name in SPANS.items():
+            pending = {}
+            for ev in evs:
+                if ev.name == b:
+                    pending[(ev.tile, ev.k_block)] = ev.t_ns
+                elif ev.name == e:
+                    key = (ev.tile, ev.k_block if b != "epi_go" else 0)
+                    if key in pending:
+                        out.append((name, pending.pop(key), ev.t_ns, ev.tile, ev.k_block))
+        return sorted(out, key=lambda s: s[1])
+
+    def summary(self) -> dict[str, Any]:
+        """Per CTA and role: elapsed time and the total/mean of each wait span."""
+
+        result: dict[str, Any] = {"shape": list(self.shape), "config": self.config, "ctas": {}}
+        for cta in sorted({e.cta for e in self.events}):
+            per_role = {}
+            for role in ROLES:
+                evs = self.role_events(cta, role)
+                if not evs:
+                    continue
+                t0 = min(e.t_ns for e in evs)
+                t1 = max(e.t_ns for e in evs)
+                totals: dict[str, list[int]] = {}
+                for name, b, e, _, _ in self.spans(cta, role):
+                    totals.setdefault(name, []).append(e - b)
+                per_role[role] = {
+                    "elapsed_us": (t1 - t0) / 1e3,
+                    "events": len(evs),
+                    "spans": {
+                        name: {"count": len(v), "total_us": sum(v) / 1e3, "mean_ns": sum(v) / len(v),
+                               "share_of_elapsed": (sum(v) / (t1 - t0)) if t1 > t0 else 0.0}
+                        for name, v in totals.items()
+                    },
+                }
+                if role == "mma":
+                    done = [e.t_ns for e in evs if e.name == "mma_tile_done"]
+                    go = [e.t_ns for e in evs if e.name == "mma_acc_go"]
+                    gaps = [g - d for d, g in zip(done, go[1:])]
+                    if gaps:
+                        per_role[role]["tile_boundary_gap_ns"] = {"mean": sum(gaps) / len(gaps), "max": max(gaps),
+                                                                  "count": len(gaps)}
+            result["ctas"][cta] = per_role
+        return result
+
+    def to_chrome_trace(self) -> dict[str, Any]:
+        t0 = min((e.t_ns for e in self.events), default=0)
+        trace_events = []
+        for cta in sorted({e.cta for e in self.events}):
+            for tid, role in enumerate(ROLES):
+                trace_events.append({"name": "thread_name", "ph": "M", "pid": cta, "tid": tid,
+                                     "args": {"name": role}})
+                for name, b, e, tile, kb in self.spans(cta, role):
+                    trace_events.append({"name": name, "ph": "X", "pid": cta, "tid": tid, "ts": (b - t0) / 1e3,
+                                         "dur": max(e - b, 1) / 1e3, "args": {"tile": tile, "k_block": kb}})
+        return {"traceEvents": trace_events, "displayTimeUnit": "ns",
+                "metadata": {"shape": list(self.shape), "config": self.config}}
+
+    def write(self, directory: str | Path, stem: str = "gemm_trace") -> dict[str, Path]:
+        directory = Path(directory)
+        directory.mkdir(parents=True, exist_ok=True)
+        paths = {"trace_json": directory / f"{stem}.trace.json", "summary": directory / f"{stem}.summary.json"}
+        paths["trace_json"].write_text(json.dumps(self.to_chrome_trace()))
+        paths["summary"].write_text(json.dumps(self.summary(), indent=1))
+        return paths
+
+
+def decode(raw, capacity: int, ctas: int = 2) -> list[Event]:
+    """Decode the flat uint64 trace buffer written by cutex_mxfp8_gemm_trace."""
+
+    events = []
+    stride = (capacity + 1) * 2
+    for cta in range(ctas):
+        for r, role in enumerate(ROLES):
+            base = (cta * 3 + r) * stride
+            count = int(raw[base])
+            for i in range(1, min(count, capacity) + 1):
+                t = int(raw[base + 2 * i])
+                info = int(raw[base + 2 * i + 1])
+                ev = EVENTS.get(info >> 56, f"event{info >> 56}")
+                events.append(Event(cta, role, t, ev, (info >> 24) & 0xFFFFFFF, info & 0xFFFFFF))
+    return events
+
+
+def run_gemm_trace(a, b, sfa, sfb, out, config=None, capacity: int = 1 << 16) -> GemmTrace:
+    """Run one instrumented GEMM launch (torch CUDA tensors) and return its decoded trace."""
+
+    import torch
+
+    from .kernels.dense_gemm import GemmConfig, _stream_handle
+
+    cfg = config or GemmConfig(kernel=2, stages=6, epi_buffers=1, sf_buffers=1)
+    buf = torch.zeros(6 * (capacity + 1) * 2, dtype=torch.int64, device=out.device)
+    m, k = a.shape
+    n = b.shape[0]
+    status = _lib.load().cutex_mxfp8_gemm_trace(
+        a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), out.data_ptr(), m, n, k, out.stride(0),
+        ctypes.byref(cfg.to_c()), buf.data_ptr(), capacity, _stream_handle(None))
+    _lib.check(status, "cutex_mxfp8_gemm_trace")
+    torch.cuda.synchronize()
+    raw = buf.cpu().numpy().view("uint64")
+    events = decode(raw, capacity)
+    if not events:
+        raise TraceError("the traced launch recorded no events")
+    return GemmTrace(events, capacity, (m, n, k), dict(cfg.__dict__))
+
+
+def disabled_trace_metadata() -> dict[str, Any]:
+    """Result-metadata stanza for runs without tracing (same role as ``disabled_iket_metadata``)."""
+
+    return {"enabled": False, "benchmark_instrumented": False, "tool": "cutex_mxfp8_gemm_trace"}
+
+
+__all__ = ["Event", "GemmTrace", "TraceError", "decode", "disabled_trace_metadata", "run_gemm_trace"]

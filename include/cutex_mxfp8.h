@@ -118,6 +118,22 @@ CUTEX_API int cutex_mxfp8_query(const cutex_gemm_config* cfg, int64_t M, int64_t
                       cutex_gemm_info* info);
 
 /*
+ * Diagnostics: the same GEMM on an instrumented build of the kernel that
+ * records per-role %globaltimer events of the first CTA (pair) into `trace`
+ * (caller-allocated, 8-byte aligned, 6 * (trace_cap + 1) * 2 uint64 values:
+ * regions [cta_rank * 3 + role], role 0 = TMA producer, 1 = MMA issuer,
+ * 2 = epilogue warp 0; record 0 of a region = event count, record i = {time_ns,
+ * event << 56 | tile << 24 | k_block}). Only configurations with an
+ * instrumented twin are accepted (CUTEX_ERR_INVALID_ARGUMENT otherwise).
+ * Replaces the reference's IKET in-kernel ranges (cutex/trace.py:96-175,
+ * cutex/kernels/dense_gemm_v9.py:116-125); benchmark builds carry no tracing.
+ */
+CUTEX_API int cutex_mxfp8_gemm_trace(const void* a, const void* b, const void* sfa, const void* sfb,
+                                     void* d, int64_t M, int64_t N, int64_t K, int64_t ldd,
+                                     const cutex_gemm_config* cfg, unsigned long long* trace,
+                                     int32_t trace_cap, cutex_stream_t stream);
+
+/*
  * The reference's fixed-shape entry: M = N = K = 16384, D row stride 16384,
  * 2-CTA persistent kernel with at most `max_active_clusters` CTA pairs
  * (<= 0: as many as fit). Mirrors `dense_gemm_v13(a_ptr, b_ptr, sfa_ptr,
