@@ -12,6 +12,7 @@
 #include "../../include/cutex_mxfp8.h"
 #include "mxfp8_gemm.cuh"
 #include "mxfp8_quant.cuh"
+#include "mxfp8_skinny.cuh"
 
 namespace cutex {
 namespace {
@@ -161,15 +162,56 @@ Variant* find_variant(int cg, int bn, int stages, int epi, int sfb) {
   return best;
 }
 
+// Skinny (M <= 128) kernels: (padded M, stages).
+struct SkinnyVariant {
+  int npad, stages, smem_bytes;
+  const void* fn;
+  bool attr_set[kMaxDevices];
+};
+
+template <int NP, int S>
+SkinnyVariant make_skinny() {
+  SkinnyVariant v{};
+  v.npad = NP;
+  v.stages = S;
+  v.smem_bytes = SkinnyCfg<NP, S>::kSmemBytes;
+  v.fn = reinterpret_cast<const void*>(&mxfp8_skinny_kernel<NP, S>);
+  return v;
+}
+
+SkinnyVariant g_skinny[] = {
+    make_skinny<16, 10>(), make_skinny<32, 10>(), make_skinny<64, 8>(), make_skinny<128, 6>(),
+};
+
+SkinnyVariant* find_skinny(int64_t M) {
+  for (auto& v : g_skinny)
+    if (M <= v.npad) return &v;
+  return nullptr;
+}
+
 struct Plan {
   Variant* variant;
+  SkinnyVariant* skinny;
   int kernel;
   int tile_n;
   int raster_group;
   int raster_along_n;
   int grid_ctas;
   int num_m_tiles, num_n_tiles, num_tiles;
+  int streamk;                // skinny: stream-K split over the grid (needs workspace)
+  int64_t workspace_bytes;    // skinny stream-K: partial slots + tile counters
+  int64_t ws_partials_bytes;  // offset of the counters inside the workspace
 };
+
+// Skinny stream-K workspace layout, fixed per device so that one workspace can
+// serve calls of any shape: a partial-sum region sized for the largest grid and
+// padded M (2 slots x sm_count CTAs x 128 x 128 fp32), then one uint32 arrival
+// counter per 128-row tile of B. Counters never alias partial slots, and every
+// completed call leaves the counters it used at zero.
+void skinny_workspace(int sm_count, int n_tiles, int64_t* partial_bytes, int64_t* total) {
+  *partial_bytes = static_cast<int64_t>(2) * sm_count * 128 * 128 * 4;
+  *total = *partial_bytes + ((static_cast<int64_t>(n_tiles) * 4 + 255) / 256) * 256;
+}
 
 bool cfg_reserved_zero(const cutex_gemm_config* cfg) {
   for (int r : cfg->reserved)
@@ -198,8 +240,38 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
     return CUTEX_ERR_INVALID_ARGUMENT;
   if (cfg.tile_n != 0 && cfg.tile_n != 128 && cfg.tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
   int kernel = cfg.kernel;
-  if (kernel == CUTEX_KERNEL_SKINNY) return CUTEX_ERR_INVALID_ARGUMENT;  // not built yet
-  if (kernel == CUTEX_KERNEL_AUTO) kernel = (M > 128 && N % 256 == 0) ? CUTEX_KERNEL_2CTA : CUTEX_KERNEL_1CTA;
+  if (kernel == CUTEX_KERNEL_AUTO) {
+    if (M <= 128) kernel = CUTEX_KERNEL_SKINNY;
+    else kernel = (N % 256 == 0) ? CUTEX_KERNEL_2CTA : CUTEX_KERNEL_1CTA;
+  }
+  plan->skinny = nullptr;
+  plan->variant = nullptr;
+  plan->streamk = 0;
+  plan->workspace_bytes = 0;
+  plan->ws_partials_bytes = 0;
+  if (kernel == CUTEX_KERNEL_SKINNY) {
+    SkinnyVariant* sv = find_skinny(M);
+    if (sv == nullptr) return CUTEX_ERR_SHAPE;  // the skinny kernel covers M <= 128
+    if (cfg.stages != 0 && cfg.stages != sv->stages) return CUTEX_ERR_INVALID_ARGUMENT;
+    if (cfg.split_k > 1) return CUTEX_ERR_INVALID_ARGUMENT;  // 0 = stream-K, 1 = no split
+    plan->skinny = sv;
+    plan->kernel = kernel;
+    plan->tile_n = 128;
+    plan->num_m_tiles = 1;
+    plan->num_n_tiles = static_cast<int>((N + 127) / 128);
+    plan->num_tiles = plan->num_n_tiles;
+    plan->raster_group = 1;
+    plan->raster_along_n = 0;
+    const int64_t units = static_cast<int64_t>(plan->num_n_tiles) * (K / 128);
+    int grid = sm_count;
+    if (cfg.max_ctas != 0) grid = std::min(grid, cfg.max_ctas);
+    plan->streamk = cfg.split_k == 1 ? 0 : 1;
+    grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, plan->streamk ? units : plan->num_n_tiles)));
+    plan->grid_ctas = grid;
+    if (plan->streamk)
+      skinny_workspace(sm_count, plan->num_n_tiles, &plan->ws_partials_bytes, &plan->workspace_bytes);
+    return CUTEX_OK;
+  }
   int tile_n = cfg.tile_n;
   if (kernel == CUTEX_KERNEL_2CTA) {
     if (tile_n == 0) tile_n = 256;
@@ -296,6 +368,46 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
   return CUTEX_OK;
 }
 
+int launch_skinny(const Plan& plan, int dev, const void* a, const void* b, const void* sfa,
+                  const void* sfb, void* d, int64_t M, int64_t N, int64_t K, int64_t ldd,
+                  void* workspace, cudaStream_t stream) {
+  SkinnyVariant* v = plan.skinny;
+  CUtensorMap tb, ta, tsb, tsa;
+  if (!encode_operand(&tb, b, N, K, 128) || !encode_operand(&ta, a, M, K, static_cast<uint32_t>(v->npad)) ||
+      !encode_scales(&tsb, sfb, N, K, 1) || !encode_scales(&tsa, sfa, M, K, 1))
+    return CUTEX_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!v->attr_set[dev]) {
+      if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v->smem_bytes) !=
+          cudaSuccess)
+        return CUTEX_ERR_CUDA;
+      v->attr_set[dev] = true;
+    }
+  }
+  SkinnyArgs args{};
+  args.M = static_cast<int>(M);
+  args.N = static_cast<int>(N);
+  args.num_n_tiles = plan.num_n_tiles;
+  args.num_k_blocks = static_cast<int>(K / 128);
+  args.units = static_cast<long long>(plan.num_n_tiles) * args.num_k_blocks;
+  args.streamk = plan.streamk;
+  args.ldd = ldd;
+  args.d = static_cast<__nv_bfloat16*>(d);
+  args.partials = plan.streamk ? static_cast<float*>(workspace) : nullptr;
+  args.counters = plan.streamk
+                      ? reinterpret_cast<unsigned int*>(static_cast<char*>(workspace) + plan.ws_partials_bytes)
+                      : nullptr;
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(static_cast<unsigned>(plan.grid_ctas), 1, 1);
+  lc.blockDim = dim3(192, 1, 1);
+  lc.dynamicSmemBytes = static_cast<size_t>(v->smem_bytes);
+  lc.stream = stream;
+  void* params[] = {&tb, &ta, &tsb, &tsa, &args};
+  if (cudaLaunchKernelExC(&lc, v->fn, params) != cudaSuccess) return CUTEX_ERR_CUDA;
+  return CUTEX_OK;
+}
+
 }  // namespace
 }  // namespace cutex
 
@@ -314,18 +426,30 @@ extern "C" int cutex_mxfp8_query(const cutex_gemm_config* cfg, int64_t M, int64_
   if (rc != CUTEX_OK) return rc;
   std::memset(info, 0, sizeof(*info));
   info->kernel = plan.kernel;
+  info->tile_k = 128;
+  info->grid_ctas = plan.grid_ctas;
+  info->num_tiles = plan.num_tiles;
+  info->raster_group = plan.raster_group;
+  if (plan.skinny != nullptr) {
+    info->tile_m = plan.skinny->npad;  // padded M: the MMA's N side
+    info->tile_n = 128;
+    info->stages = plan.skinny->stages;
+    info->cluster_size = 1;
+    info->smem_bytes = plan.skinny->smem_bytes;
+    info->split_k = plan.streamk ? 0 : 1;  // 0: stream-K over the grid
+    info->epi_buffers = 0;
+    info->sf_buffers = 2;
+    info->workspace_bytes = plan.workspace_bytes;
+    return CUTEX_OK;
+  }
   info->tile_m = 128 * plan.variant->cta_group;
   info->tile_n = plan.tile_n;
-  info->tile_k = 128;
   info->stages = plan.variant->stages;
   info->cluster_size = plan.variant->cta_group;
-  info->grid_ctas = plan.grid_ctas;
   info->smem_bytes = plan.variant->smem_bytes;
-  info->num_tiles = plan.num_tiles;
   info->split_k = 1;
   info->epi_buffers = plan.variant->epi_bufs;
   info->sf_buffers = plan.variant->sf_bufs;
-  info->raster_group = plan.raster_group;
   info->workspace_bytes = 0;
   return CUTEX_OK;
 }
@@ -351,6 +475,20 @@ extern "C" int cutex_mxfp8_gemm(const void* a, const void* b, const void* sfa, c
   if (st != CUTEX_OK) return st;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
+  if (plan.skinny != nullptr) {
+    if (plan.streamk && (workspace == nullptr || workspace_bytes < plan.workspace_bytes)) {
+      // Explicit stream-K needs the workspace; AUTO without one takes whole tiles instead.
+      if (cfg != nullptr && cfg->kernel == CUTEX_KERNEL_SKINNY) return CUTEX_ERR_WORKSPACE;
+      cutex_gemm_config whole = cfg != nullptr ? *cfg : cutex_gemm_config{};
+      whole.kernel = CUTEX_KERNEL_SKINNY;
+      whole.split_k = 1;
+      st = resolve_plan(&whole, M, N, K, ds->sm_count, &plan);
+      if (st != CUTEX_OK) return st;
+    }
+    if (plan.streamk && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return CUTEX_ERR_ALIGN;
+    return launch_skinny(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd, workspace,
+                         reinterpret_cast<cudaStream_t>(stream));
+  }
   return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd,
                      reinterpret_cast<cudaStream_t>(stream));
 }
@@ -375,6 +513,7 @@ extern "C" int cutex_mxfp8_gemm_trace(const void* a, const void* b, const void* 
   Plan plan{};
   st = resolve_plan(cfg, M, N, K, ds->sm_count, &plan);
   if (st != CUTEX_OK) return st;
+  if (plan.variant == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;  // no traced skinny build
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
   return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd,

@@ -278,6 +278,7 @@ __global__ void __launch_bounds__(192, 1)
         const int b_row = nt * kTileN + static_cast<int>(rank) * C::kLoadN;
         const int sfa_blk = a_row / 128;
         const int sfb_blk = (nt * kTileN) / 128;
+        const uint64_t pol = ptx::policy_evict_normal();
         for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
           const int s = static_cast<int>(kit % kStages);
           const uint32_t round = kit / kStages;
@@ -295,16 +296,16 @@ __global__ void __launch_bounds__(192, 1)
           const int kx = kb * 128;
           if constexpr (kPair) {
             const uint32_t fb = ptx::mapa(full_bar(s), 0);
-            ptx::tma_load_2d_pair(sa, &tmap_a, fb, kx, a_row, ptx::kEvictNormal);
-            ptx::tma_load_2d_pair(sb, &tmap_b, fb, kx, b_row, ptx::kEvictNormal);
-            ptx::tma_load_3d_pair(ssfa, &tmap_sfa, fb, 0, kb, sfa_blk, ptx::kEvictNormal);
-            ptx::tma_load_3d_pair(ssfb, &tmap_sfb, fb, 0, kb, sfb_blk, ptx::kEvictNormal);
+            ptx::tma_load_2d_pair(sa, &tmap_a, fb, kx, a_row, pol);
+            ptx::tma_load_2d_pair(sb, &tmap_b, fb, kx, b_row, pol);
+            ptx::tma_load_3d_pair(ssfa, &tmap_sfa, fb, 0, kb, sfa_blk, pol);
+            ptx::tma_load_3d_pair(ssfb, &tmap_sfb, fb, 0, kb, sfb_blk, pol);
           } else {
             const uint32_t fb = full_bar(s);
-            ptx::tma_load_2d(sa, &tmap_a, fb, kx, a_row, ptx::kEvictNormal);
-            ptx::tma_load_2d(sb, &tmap_b, fb, kx, b_row, ptx::kEvictNormal);
-            ptx::tma_load_3d(ssfa, &tmap_sfa, fb, 0, kb, sfa_blk, ptx::kEvictNormal);
-            ptx::tma_load_3d(ssfb, &tmap_sfb, fb, 0, kb, sfb_blk, ptx::kEvictNormal);
+            ptx::tma_load_2d(sa, &tmap_a, fb, kx, a_row, pol);
+            ptx::tma_load_2d(sb, &tmap_b, fb, kx, b_row, pol);
+            ptx::tma_load_3d(ssfa, &tmap_sfa, fb, 0, kb, sfa_blk, pol);
+            ptx::tma_load_3d(ssfb, &tmap_sfb, fb, 0, kb, sfb_blk, pol);
           }
         }
       }

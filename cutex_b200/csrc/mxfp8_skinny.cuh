@@ -1,0 +1,320 @@
+// Skinny MXFP8 GEMM (M <= 128): HBM-bound streaming of B with swapped operands.
+//
+//   D[M,N] = A[M,K] . B[N,K]^T  is computed as  D^T[N,M] = B . A^T :
+//   the MMA's 128-row side walks 128-row tiles of B (N), its N side is the
+//   padded M (kNPad = 16..128). B is read once from HBM (evict-first), A and its
+//   scales stay L2-resident (evict-last) and are re-read per K-stage.
+//
+// Work split (stream-K): the (N-tile, K-stage) units are cut into gridDim.x
+// equal contiguous ranges, one per CTA, so every SM streams the same number of
+// bytes. A CTA that covers a whole tile writes BF16 D directly. A tile cut
+// between CTAs is finished through a workspace: each contributor stores its
+// FP32 partial in its own slot, then increments the tile's arrival counter; the
+// contributor that arrives last sums all partials in contributor order
+// (deterministic), writes D, and resets the counter to zero for the next call.
+// Nobody waits for another CTA. Without a workspace (split disabled) CTAs take
+// whole tiles round-robin.
+//
+// Warp roles (192 threads) as in the large kernel: warps 0-3 epilogue (TMEM lane
+// quarter w = rows 32w..32w+31 of the B tile), warp 4 MMA issuer, warp 5 TMA.
+// TMEM: two kNPad-column accumulators (per segment, alternating) + scale
+// columns (MMA-A scales = B's chunk, MMA-B scales = A's chunk) in two buffers.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "mxfp8_gemm.cuh"
+#include "ptx.cuh"
+
+namespace cutex {
+
+struct SkinnyArgs {
+  int M;              // rows of A (<= kNPad)
+  int N;              // rows of B
+  int num_n_tiles;    // ceil(N / 128)
+  int num_k_blocks;   // K / 128
+  long long units;    // num_n_tiles * num_k_blocks
+  int streamk;        // 1: stream-K split over gridDim.x CTAs; 0: whole tiles round-robin
+  long long ldd;      // row stride of D (elements)
+  __nv_bfloat16* d;
+  float* partials;    // [2 * gridDim.x][kNPad][128] fp32 slots (stream-K only)
+  unsigned int* counters;  // [num_n_tiles] arrival counters, zero between calls
+};
+
+template <int kNPad, int kStages>
+struct SkinnyCfg {
+  static constexpr int kBBytes = 128 * 128;        // one 128-row x 128-K tile of B
+  static constexpr int kABytes = kNPad * 128;      // kNPad rows of A
+  static constexpr int kStageBytes = kBBytes + kABytes + 512 + 512;
+  static constexpr int kOffB = 0;
+  static constexpr int kOffA = kOffB + kStages * kBBytes;
+  static constexpr int kOffSFB = kOffA + kStages * kABytes;  // B's scale chunk (MMA A side)
+  static constexpr int kOffSFA = kOffSFB + kStages * 512;    // A's scale chunk (MMA B side)
+  static constexpr int kOffBar = align_up(kOffSFA + kStages * 512, 8);
+  static constexpr int kNumBars = 2 * kStages + 4;
+  static constexpr int kOffSlot = kOffBar + kNumBars * 8;  // TMEM address + last-arrival flag
+  static constexpr int kSmemBytes = kOffSlot + 16 + 1024;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kAcc1Col = 128;
+  static constexpr int kSFCol = 256;  // two buffers of 8 columns: [B chunk 4 | A chunk 4]
+  static constexpr uint32_t kTxBytes = kStageBytes;
+  static constexpr uint32_t kIdesc = ptx::mxf8_idesc(128, kNPad);
+  static_assert(kNPad % 16 == 0 && kNPad >= 16 && kNPad <= 128, "padded M");
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
+};
+
+// Units [start(c), start(c+1)) of CTA c.
+__device__ __forceinline__ long long sk_start(long long c, long long P, long long U) {
+  return c * U / P;
+}
+
+// CTA whose range holds unit u: the largest c with start(c) <= u.
+__device__ __forceinline__ long long sk_owner(long long u, long long P, long long U) {
+  return ((u + 1) * P - 1) / U;
+}
+
+// Walks a CTA's segments: (tile, first K-stage, end K-stage) in order.
+struct SegmentWalker {
+  long long u, u_end;
+  int tile_rr;  // round-robin tile for the non-split mode
+  __device__ __forceinline__ void init(const SkinnyArgs& a) {
+    if (a.streamk) {
+      u = sk_start(blockIdx.x, gridDim.x, a.units);
+      u_end = sk_start(blockIdx.x + 1, gridDim.x, a.units);
+    } else {
+      tile_rr = blockIdx.x;
+      u = 0;
+      u_end = 0;
+    }
+  }
+  __device__ __forceinline__ bool next(const SkinnyArgs& a, int& tile, int& kb0, int& kb1) {
+    if (a.streamk) {
+      if (u >= u_end) return false;
+      tile = static_cast<int>(u / a.num_k_blocks);
+      kb0 = static_cast<int>(u - static_cast<long long>(tile) * a.num_k_blocks);
+      const long long left = u_end - u;
+      kb1 = static_cast<int>(min(static_cast<long long>(a.num_k_blocks), kb0 + left));
+      u += kb1 - kb0;
+      return true;
+    }
+    if (tile_rr >= a.num_n_tiles) return false;
+    tile = tile_rr;
+    tile_rr += gridDim.x;
+    kb0 = 0;
+    kb1 = a.num_k_blocks;
+    return true;
+  }
+};
+
+template <int kNPad, int kStages>
+__global__ void __launch_bounds__(192, 1)
+    mxfp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,
+                        const __grid_constant__ CUtensorMap tmap_a,
+                        const __grid_constant__ CUtensorMap tmap_sfb,
+                        const __grid_constant__ CUtensorMap tmap_sfa, const SkinnyArgs args) {
+  using C = SkinnyCfg<kNPad, kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = ptx::smem_u32(smem_raw);
+  const uint32_t smem = (raw_base + 1023u) & ~1023u;
+  uint8_t* smem_ptr = smem_raw + (smem - raw_base);
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = ptx::lane_id();
+  int* status = &g_cutex_device_status;
+
+  const uint32_t bar0 = smem + C::kOffBar;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
+  auto acc_full_bar = [&](int b) { return bar0 + 8u * (2 * kStages + b); };
+  auto acc_empty_bar = [&](int b) { return bar0 + 8u * (2 * kStages + 2 + b); };
+  volatile uint32_t* slot = reinterpret_cast<volatile uint32_t*>(smem_ptr + C::kOffSlot);
+
+  if (warp == 5 && lane == 0) {
+    ptx::prefetch_tmap(&tmap_b);
+    ptx::prefetch_tmap(&tmap_a);
+    ptx::prefetch_tmap(&tmap_sfb);
+    ptx::prefetch_tmap(&tmap_sfa);
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(full_bar(s), 1);
+      ptx::mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(acc_full_bar(b), 1);
+      ptx::mbar_init(acc_empty_bar(b), 4);
+    }
+    ptx::fence_mbar_init();
+  }
+  if (warp == 4) {
+    ptx::tmem_alloc<1>(ptx::smem_u32(const_cast<uint32_t*>(slot)), C::kTmemCols);
+    ptx::tmem_relinquish<1>();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = slot[0];
+
+  SegmentWalker walk;
+  walk.init(args);
+  int tile, kb0, kb1;
+
+  if (warp == 5) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t stream_pol = ptx::policy_evict_first();
+      const uint64_t keep_pol = ptx::policy_evict_last();
+      uint32_t kit = 0;
+      bool ok = true;
+      while (ok && walk.next(args, tile, kb0, kb1)) {
+        for (int kb = kb0; kb < kb1; ++kb, ++kit) {
+          const int s = static_cast<int>(kit % kStages);
+          if (!ptx::mbar_wait(empty_bar(s), ((kit / kStages) & 1u) ^ 1u, status, kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar(s);
+          ptx::mbar_arrive_expect_tx(fb, C::kTxBytes);
+          ptx::tma_load_2d(smem + C::kOffB + s * C::kBBytes, &tmap_b, fb, kb * 128, tile * 128, stream_pol);
+          ptx::tma_load_2d(smem + C::kOffA + s * C::kABytes, &tmap_a, fb, kb * 128, 0, keep_pol);
+          ptx::tma_load_3d(smem + C::kOffSFB + s * 512, &tmap_sfb, fb, 0, kb, tile, stream_pol);
+          ptx::tma_load_3d(smem + C::kOffSFA + s * 512, &tmap_sfa, fb, 0, kb, 0, keep_pol);
+        }
+      }
+      for (int i = 0; ok && i < kStages; ++i) {
+        const uint32_t k2 = kit + i;
+        ok = ptx::mbar_wait(empty_bar(static_cast<int>(k2 % kStages)), ((k2 / kStages) & 1u) ^ 1u, status,
+                            kDevTimeoutProducer);
+      }
+      if (!ok) settle_inflight_copies();
+    }
+    __syncwarp();
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t kit = 0;
+      int seg = 0;
+      bool ok = true;
+      while (ok && walk.next(args, tile, kb0, kb1)) {
+        const int buf = seg & 1;
+        if (seg >= 2 &&
+            !ptx::mbar_wait(acc_empty_bar(buf), ((seg - 2) >> 1) & 1, status, kDevTimeoutAccEmpty))
+          break;
+        ptx::tc_fence_after();
+        const uint32_t d_t = tmem_base + (buf ? C::kAcc1Col : 0);
+        for (int kb = kb0; kb < kb1; ++kb, ++kit) {
+          const int s = static_cast<int>(kit % kStages);
+          if (!ptx::mbar_wait(full_bar(s), (kit / kStages) & 1u, status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sf_t = tmem_base + C::kSFCol + (kit & 1u) * 8u;
+          ptx::tmem_cp_32x128b_x4<1>(sf_t, ptx::sf_chunk_desc(smem + C::kOffSFB + s * 512));
+          ptx::tmem_cp_32x128b_x4<1>(sf_t + 4, ptx::sf_chunk_desc(smem + C::kOffSFA + s * 512));
+          const uint64_t a_desc = ptx::kmajor_sw128_desc(smem + C::kOffB + s * C::kBBytes);
+          const uint64_t b_desc = ptx::kmajor_sw128_desc(smem + C::kOffA + s * C::kABytes);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            ptx::mma_mxf8f6f4<1>(d_t, a_desc + 2 * j, b_desc + 2 * j, ptx::with_scale_id(C::kIdesc, j),
+                                 sf_t | (static_cast<uint32_t>(j) << 30),
+                                 (sf_t + 4) | (static_cast<uint32_t>(j) << 30),
+                                 (kb != kb0 || j != 0) ? 1u : 0u);
+          }
+          ptx::tc_commit<1>(empty_bar(s));
+        }
+        if (!ok) break;
+        ptx::tc_commit<1>(acc_full_bar(buf));
+        ++seg;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int P = gridDim.x;
+    const long long U = args.units;
+    const int first_tile =
+        args.streamk ? static_cast<int>(sk_start(blockIdx.x, P, U) / args.num_k_blocks) : -1;
+    const uint32_t tid = threadIdx.x;  // 0..127: row of the B tile = column of D
+    int seg = 0;
+    while (walk.next(args, tile, kb0, kb1)) {
+      const int buf = seg & 1;
+      if (!ptx::mbar_wait(acc_full_bar(buf), (seg >> 1) & 1, status, kDevTimeoutEpilogue)) break;
+      ptx::tc_fence_after();
+      const uint32_t acc = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) +
+                           static_cast<uint32_t>(buf ? C::kAcc1Col : 0);
+      const bool whole = kb0 == 0 && kb1 == args.num_k_blocks;
+      const int n = tile * 128 + static_cast<int>(tid);
+      float* part = nullptr;
+      if (!whole) {
+        const int s = (tile == first_tile) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+        part = args.partials + static_cast<size_t>(s) * kNPad * 128;
+      }
+#pragma unroll 1
+      for (int c = 0; c < kNPad; c += 16) {
+        uint32_t v[16];
+        ptx::tmem_ld_32x32b_x16(acc + c, v);
+        ptx::tmem_wait_ld();
+        if (whole) {
+          if (n < args.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (c + j < args.M)
+                args.d[static_cast<long long>(c + j) * args.ldd + n] = __float2bfloat16_rn(__uint_as_float(v[j]));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) part[(c + j) * 128 + tid] = __uint_as_float(v[j]);
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(acc_empty_bar(buf));
+      if (!whole) {
+        // Publish the partial, count arrivals; the last contributor reduces.
+        __threadfence();
+        ptx::named_barrier(1, 128);
+        const long long t_u0 = static_cast<long long>(tile) * args.num_k_blocks;
+        const int c0 = static_cast<int>(sk_owner(t_u0, P, U));
+        const int c1 = static_cast<int>(sk_owner(t_u0 + args.num_k_blocks - 1, P, U));
+        if (tid == 0) {
+          const unsigned int prev = atomicAdd(&args.counters[tile], 1u);
+          slot[1] = (prev == static_cast<unsigned int>(c1 - c0)) ? 1u : 0u;
+        }
+        ptx::named_barrier(1, 128);
+        if (slot[1] != 0u) {
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < kNPad; c += 16) {
+            float sum[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sum[j] = 0.f;
+            for (int cc = c0; cc <= c1; ++cc) {
+              const int ft = static_cast<int>(sk_start(cc, P, U) / args.num_k_blocks);
+              const int s = (ft == tile) ? 2 * cc : 2 * cc + 1;
+              const float* src = args.partials + static_cast<size_t>(s) * kNPad * 128;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) sum[j] += __ldcg(src + (c + j) * 128 + tid);
+            }
+            if (n < args.N) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                if (c + j < args.M)
+                  args.d[static_cast<long long>(c + j) * args.ldd + n] = __float2bfloat16_rn(sum[j]);
+            }
+          }
+          if (tid == 0) args.counters[tile] = 0u;
+        }
+        ptx::named_barrier(1, 128);
+      }
+      ++seg;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc<1>(tmem_base, C::kTmemCols);
+  }
+}
+
+}  // namespace cutex

@@ -74,8 +74,34 @@ def query(m: int, n: int, k: int, config: GemmConfig | None = None) -> dict[str,
     return {name: getattr(info, name) for name, _ in _lib.GemmInfoC._fields_}
 
 
+_WORKSPACES: dict[tuple[int, int], Any] = {}
+
+
+def workspace_for(device, stream_handle: int, nbytes: int):
+    """A zero-initialised device workspace of at least ``nbytes``, cached per (device, stream).
+
+    The split-K skinny kernel leaves its arrival counters at zero when it
+    finishes, so one workspace serves every later call on the same stream
+    (calls on different streams get different workspaces: they may overlap).
+    """
+
+    import torch
+
+    key = (int(device.index if device.index is not None else torch.cuda.current_device()), int(stream_handle))
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
 def dense_gemm(a, b, sfa, sfb, out, stream=None, config: GemmConfig | None = None, workspace=None):
-    """D = dequant(A, SFA) @ dequant(B, SFB)^T in BF16 (FP32 accumulate); launches asynchronously."""
+    """D = dequant(A, SFA) @ dequant(B, SFB)^T in BF16 (FP32 accumulate); launches asynchronously.
+
+    Shapes with M <= 128 run the split-K skinny kernel, which needs a device
+    workspace (``query(...)["workspace_bytes"]``); when ``workspace`` is None a
+    zero-initialised one is allocated once per (device, stream) and reused.
+    """
 
     import torch
 
@@ -97,10 +123,15 @@ def dense_gemm(a, b, sfa, sfb, out, stream=None, config: GemmConfig | None = Non
     if sfb.numel() * sfb.element_size() < scale_buffer_bytes(n, k):
         raise ValueError(f"sfb holds {sfb.numel()} bytes; {scale_buffer_bytes(n, k)} required")
     cfg = (config or GemmConfig()).to_c()
+    handle = _stream_handle(stream)
+    if workspace is None and m <= 128:
+        need = query(m, n, k, config)["workspace_bytes"]
+        if need > 0:
+            workspace = workspace_for(a.device, handle, need)
     ws_ptr, ws_bytes = (0, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
     status = _lib.load().cutex_mxfp8_gemm(
         a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), out.data_ptr(),
-        m, n, k, out.stride(0), ctypes.byref(cfg), ws_ptr or None, ws_bytes, _stream_handle(stream),
+        m, n, k, out.stride(0), ctypes.byref(cfg), ws_ptr or None, ws_bytes, handle,
     )
     _lib.check(status, "cutex_mxfp8_gemm")
     return out
@@ -166,4 +197,5 @@ __all__ = [
     "device_target",
     "mxfp8_gemm_launch",
     "query",
+    "workspace_for",
 ]

@@ -66,7 +66,7 @@ typedef struct cutex_gemm_config {
   int32_t stages;         /* shared-memory ring depth */
   int32_t raster_group;   /* output tiles per rasterisation group (>= 1) */
   int32_t raster_along_n; /* 0: walk M inside a group, 1: walk N inside a group */
-  int32_t split_k;        /* skinny kernel: K splits (0 = auto) */
+  int32_t split_k;        /* skinny kernel: 0 = stream-K split over all SMs, 1 = no split */
   int32_t max_ctas;       /* cap on persistent CTAs (0 = one per SM) */
   int32_t epi_buffers;    /* epilogue staging buffers per warp (1 or 2) */
   int32_t sf_buffers;     /* rotating scale-factor TMEM buffers (1, 2 or 4) */
@@ -100,9 +100,16 @@ typedef struct cutex_gemm_info {
  * shape, output stride and tile configuration as runtime arguments.
  *   a, b, d: 16-byte aligned. sfa, sfb: 16-byte aligned.
  *   K % 128 == 0, K >= 128; N % 16 == 0; ldd >= N and ldd % 8 == 0; M >= 1.
- *   workspace: device buffer of at least cutex_mxfp8_query(...)->workspace_bytes
- *   (may be NULL when that is 0). Contents need not be initialised; the call
- *   leaves it all-zero again on return of the kernel.
+ *   workspace: only the M <= 128 (skinny) kernel uses one, for split-K partial
+ *   sums and per-tile arrival counters: at least
+ *   cutex_mxfp8_query(...)->workspace_bytes, 256-byte aligned, zero-filled once
+ *   before its first use (cudaMemsetAsync); every completed call leaves it
+ *   ready for the next one, whatever the next call's shape (the layout is fixed
+ *   per device: 2 * SMs * 64 KiB of partial sums, then 4 bytes per 128 rows of
+ *   N of arrival counters). Calls that may overlap on the GPU need separate
+ *   workspaces. With the AUTO kernel and no (or a too small) workspace, M <= 128
+ *   runs without the split (whole 128-row tiles per CTA); an explicit
+ *   CUTEX_KERNEL_SKINNY config without the workspace returns CUTEX_ERR_WORKSPACE.
  */
 CUTEX_API int cutex_mxfp8_gemm(const void* a, const void* b, const void* sfa, const void* sfb, void* d,
                      int64_t M, int64_t N, int64_t K, int64_t ldd,

@@ -108,4 +108,13 @@ def test_python_wrapper_rejects_with_value_errors():
         query(256, 256, 200)
     with pytest.raises(ValueError):
         query(256, 256, 256, GemmConfig(tile_n=64))
-    assert query(16, 28672, 8192)["tile_m"] == 128
+    q = query(16, 28672, 8192)
+    assert q["kernel"] == _lib.KERNEL_SKINNY and q["tile_m"] == 16 and q["split_k"] == 0
+    assert q["workspace_bytes"] == 2 * 148 * 128 * 128 * 4 + 1024  # CPU-side default of 148 SMs
+    assert query(128, 28672, 8192)["tile_m"] == 128
+    assert query(100, 256, 256, GemmConfig(split_k=1))["workspace_bytes"] == 0
+    assert query(129, 256, 256)["kernel"] != _lib.KERNEL_SKINNY
+    with pytest.raises(ValueError):
+        query(200, 256, 256, GemmConfig(kernel=_lib.KERNEL_SKINNY))
+    with pytest.raises(ValueError):
+        query(16, 256, 256, GemmConfig(kernel=_lib.KERNEL_SKINNY, split_k=2))
