@@ -96,6 +96,7 @@ SIGNATURES = {
         [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.POINTER(GemmConfigC), _vp, _i32, _vp],
     ),
     "cutex_dense_gemm_v13": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _vp]),
+    "cutex_mxfp8_gemm_skinny_static": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "cutex_mxfp8_quantize": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
     "cutex_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "cutex_last_device_status": (ctypes.c_int, [_vp]),

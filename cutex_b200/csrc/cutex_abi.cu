@@ -585,3 +585,93 @@ extern "C" int cutex_device_sm_count(int32_t* sm_count) {
 }
 
 extern "C" const char* cutex_version(void) { return "cutex-b200 0.1.0 sm_100a"; }
+
+// ---------------------------------------------------------------------------
+// No-allocation entry point for the split-K skinny GEMM.
+//
+// Some callers cannot allocate device memory at the point where they launch a
+// GEMM: code running inside a memory-capped pool or a custom allocator that
+// forbids out-of-band cudaMalloc, real-time loops that must not hit the driver
+// allocator, and plugins that are handed only the operand and output buffers.
+// For them the skinny kernel's split-K workspace lives in a file-scope device
+// array that the library owns. The array exists once per device for as long as
+// the library is loaded: every GPU on which this library's module is loaded
+// holds these 20.06 MiB until the process exits.
+//
+// Layout (same as the caller-provided workspace): partial sums for up to 160
+// SMs x 2 slots x 128 x 128 fp32 (20 MiB), then 64 KiB of arrival counters,
+// one uint32 per 128 rows of N (N <= 2,097,152).
+namespace cutex {
+namespace {
+
+constexpr int64_t kStaticScratchPartialBytes = int64_t{2} * 160 * 128 * 128 * 4;
+constexpr int64_t kStaticScratchCounterBytes = int64_t{64} * 1024;
+
+}  // namespace
+}  // namespace cutex
+
+static __device__ __align__(256) unsigned char
+    g_skinny_static_scratch[cutex::kStaticScratchPartialBytes + cutex::kStaticScratchCounterBytes];
+
+namespace cutex {
+namespace {
+
+void* g_static_scratch_ptr[kMaxDevices];
+
+}  // namespace
+}  // namespace cutex
+
+extern "C" int cutex_mxfp8_gemm_skinny_static(const void* a, const void* b, const void* sfa,
+                                              const void* sfb, void* d, int64_t M, int64_t N,
+                                              int64_t K, int64_t ldd, cutex_stream_t stream) {
+  if (a == nullptr || b == nullptr || sfa == nullptr || sfb == nullptr || d == nullptr)
+    return CUTEX_ERR_INVALID_ARGUMENT;
+  int st = validate_shape(M, N, K);
+  if (st != CUTEX_OK) return st;
+  if (M > 128) return CUTEX_ERR_SHAPE;  // only the skinny kernel uses scratch memory
+  if (ldd < N || ldd % 8 != 0 || ldd > kMaxDim) return CUTEX_ERR_ALIGN;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(sfa) || !aligned16(sfb) || !aligned16(d))
+    return CUTEX_ERR_ALIGN;
+  DeviceState* ds = nullptr;
+  st = current_device_state(&ds);
+  if (st != CUTEX_OK) return st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
+
+  // Set-up, once per device and with that device current: in host code the
+  // array's name is only a host-side stand-in, so fetch its device address.
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (g_static_scratch_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_skinny_static_scratch) != cudaSuccess || p == nullptr)
+        return CUTEX_ERR_CUDA;
+      g_static_scratch_ptr[dev] = p;
+    }
+    scratch = g_static_scratch_ptr[dev];
+  }
+
+  cutex_gemm_config cfg{};
+  cfg.kernel = CUTEX_KERNEL_SKINNY;  // split_k = 0: stream-K over all SMs
+  Plan plan{};
+  st = resolve_plan(&cfg, M, N, K, ds->sm_count, &plan);
+  if (st != CUTEX_OK) return st;
+  // Limits of the fixed array, checked separately: at most 160 SMs of partial
+  // slots and 16384 counters (N <= 2,097,152).
+  const int64_t counter_bytes = plan.workspace_bytes - plan.ws_partials_bytes;
+  if (plan.ws_partials_bytes > kStaticScratchPartialBytes ||
+      static_cast<int64_t>(plan.num_n_tiles) * 4 > kStaticScratchCounterBytes ||
+      counter_bytes > kStaticScratchCounterBytes)
+    return CUTEX_ERR_WORKSPACE;
+
+  // The array keeps the previous call's contents; the arrival counters must
+  // start at zero, so clear the ones this call uses (the partial sums need no
+  // clearing). This is a memset on stream order, not an allocation.
+  if (cudaMemsetAsync(static_cast<char*>(scratch) + plan.ws_partials_bytes, 0,
+                      static_cast<size_t>(counter_bytes),
+                      reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return CUTEX_ERR_CUDA;
+  return launch_skinny(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd, scratch,
+                       reinterpret_cast<cudaStream_t>(stream));
+}

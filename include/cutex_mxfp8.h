@@ -165,6 +165,26 @@ CUTEX_API int cutex_dense_gemm_v13(const void* a, const void* b, const void* sfa
 CUTEX_API int cutex_mxfp8_quantize(const void* x, int32_t x_dtype, int64_t rows, int64_t K, int64_t ldx,
                          void* q, void* sf, cutex_stream_t stream);
 
+/*
+ * MXFP8 GEMM for M <= 128 that allocates nothing and takes no workspace.
+ * No counterpart in the reference. For callers that cannot call cudaMalloc at
+ * launch time (memory-capped pools, allocators that forbid out-of-band
+ * allocations, plugins handed only their operand and output buffers): the
+ * split-K skinny kernel runs with its scratch in a fixed device array owned by
+ * the library (20 MiB of partial sums + 64 KiB of counters, held on every GPU
+ * where the library is loaded until the process exits). Same operands, layout
+ * rules and result as cutex_mxfp8_gemm with the split-K skinny kernel.
+ *   M <= 128 (else CUTEX_ERR_SHAPE); N <= 2,097,152 and at most 160 SMs (else
+ *   CUTEX_ERR_WORKSPACE). The first call on a device performs one-time set-up
+ *   (it looks up the scratch array's device address); make that first call
+ *   before any stream capture. Every call shares the one scratch array: calls
+ *   that may overlap on the GPU (different streams, or different host threads)
+ *   race and must be serialised by the caller.
+ */
+CUTEX_API int cutex_mxfp8_gemm_skinny_static(const void* a, const void* b, const void* sfa,
+                                             const void* sfb, void* d, int64_t M, int64_t N,
+                                             int64_t K, int64_t ldd, cutex_stream_t stream);
+
 /* Human-readable text for a cutex_status value (static storage). */
 CUTEX_API const char* cutex_status_string(int status);
 
