@@ -53,6 +53,9 @@ def parse_args():
     p.add_argument("--allgather", action="store_true", help="also time the NCCL all-gather of D (N > 1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--config", type=str, default="", help="native config as JSON, e.g. '{\"kernel\": 2}'")
+    p.add_argument("--no-graph", action="store_true", help="plain launches instead of one CUDA graph")
+    p.add_argument("--measure-fp8-peak", action="store_true",
+                   help="measure cuBLASLt MXFP8 (torch._scaled_mm) 8192^3: best-of-10 burst and 4 s sustained")
     p.add_argument("--dist", choices=("square", "llm"), default="square",
                    help="input distribution: BASELINE square-sweep generator or LLM activations/weights")
     return p.parse_args()
@@ -305,7 +308,7 @@ def bench_cutex(args):
     import torch.distributed as dist
 
     from cutex_b200 import _lib
-    from cutex_b200.kernels import GemmConfig, dense_gemm, query
+    from cutex_b200.kernels import GemmConfig, PreparedGemm, query
     from cutex_b200.sharding import shard_bounds
 
     world, rank, local = dist_env()
@@ -324,16 +327,30 @@ def bench_cutex(args):
 
     a, sfa, b, sfb = make_operands_on_device(m, n_local, k, shard.n0, device, args.dist)
     d = torch.empty(m, n_local, dtype=torch.bfloat16, device=device)
-    stream = torch.cuda.current_stream(device)
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    torch.cuda.synchronize()
 
-    def step():
-        dense_gemm(a, b, sfa, sfb, d, stream=stream, config=cfg)
-
-    for _ in range(max(args.warmup, 3)):
-        step()
+    # One prepared C-ABI launch per step; the timed loop is a CUDA graph of `steps`
+    # launches (host launch overhead would otherwise show up as idle GPU time for
+    # the ~50 us skinny shapes), or plain launches with --no-graph.
+    with torch.cuda.stream(stream):
+        step = PreparedGemm(a, b, sfa, sfb, d, stream=stream, config=cfg)
+        for _ in range(max(args.warmup, 3)):
+            step()
     torch.cuda.synchronize()
     if _lib.load().cutex_last_device_status(stream.cuda_stream) != 0:
         raise RuntimeError("device-side timeout during warm-up")
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(args.steps):
+                step()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            graph.replay()  # first replay outside the timed region
+        torch.cuda.synchronize()
 
     sampler = ClockSampler(physical_gpu_index(local))
     sampler.start()
@@ -343,13 +360,14 @@ def bench_cutex(args):
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    per = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    start.record(stream)
-    for i in range(args.steps):
-        per[i][0].record(stream)
-        step()
-        per[i][1].record(stream)
-    end.record(stream)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(args.steps):
+                step()
+        end.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -357,8 +375,9 @@ def bench_cutex(args):
     if _lib.load().cutex_last_device_status(stream.cuda_stream) != 0:
         raise RuntimeError("device-side timeout in the timed region")
     elapsed_ms = start.elapsed_time(end)
-    launch_ms = [s.elapsed_time(e) for s, e in per]
-    t = torch.tensor([elapsed_ms, statistics.fmean(launch_ms)], dtype=torch.float64, device=device)
+    # Back-to-back launches in one graph: the average launch duration is the
+    # timed interval over the launch count (inter-kernel gaps included).
+    t = torch.tensor([elapsed_ms, elapsed_ms / args.steps], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_ms, launch_avg_ms = float(t[0]), float(t[1])
@@ -408,15 +427,17 @@ def bench_cutex(args):
             _lib.check(st, "cutex_mxfp8_gemm")
             hd.copy_(d, non_blocking=True)
 
-        e2e_step()
+        with torch.cuda.stream(stream):  # copies and the GEMM share one stream
+            e2e_step()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record(stream)
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        e2.record(stream)
+        with torch.cuda.stream(stream):
+            s2.record(stream)
+            for _ in range(args.e2e_steps):
+                e2e_step()
+            e2.record(stream)
         torch.cuda.synchronize()
         te = torch.tensor([s2.elapsed_time(e2)], dtype=torch.float64, device=device)
         if world > 1:
@@ -437,13 +458,15 @@ def bench_cutex(args):
     if args.allgather and world > 1:
         from cutex_b200.sharding import allgather_columns
 
-        allgather_columns(d, world)
+        with torch.cuda.stream(stream):
+            allgather_columns(d, world)
         torch.cuda.synchronize()
         dist.barrier()
         s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s3.record(stream)
-        full = allgather_columns(d, world)
-        e3.record(stream)
+        with torch.cuda.stream(stream):
+            s3.record(stream)
+            full = allgather_columns(d, world)
+            e3.record(stream)
         torch.cuda.synchronize()
         tg = torch.tensor([s3.elapsed_time(e3)], dtype=torch.float64, device=device)
         dist.all_reduce(tg, op=dist.ReduceOp.MAX)
@@ -502,13 +525,70 @@ def bench_cutex(args):
             line["allgather"] = allgather
         print(json.dumps(line), flush=True)
 
+    del graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
 
+def measure_fp8_peak(args):
+    """Dense FP8 denominator measured like the driver's BF16 peak: the vendor library on 8192^3.
+
+    cuBLASLt's MXFP8 GEMM through torch._scaled_mm (never part of the product
+    path): best of 10 single launches (burst) and back-to-back launches for 4 s
+    (sustained, power-capped)."""
+
+    import torch
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    n = 8192
+    a, sfa, b, sfb = make_operands_on_device(n, n, n, 0, dev)
+    A, B = a.view(torch.float8_e4m3fn), b.view(torch.float8_e4m3fn)
+    SA, SB = sfa.view(torch.float8_e8m0fnu), sfb.view(torch.float8_e8m0fnu)
+    fn = lambda: torch._scaled_mm(A, B.t(), SA, SB, out_dtype=torch.bfloat16)  # noqa: E731
+    flops = 2.0 * n ** 3
+    for _ in range(10):
+        fn()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    sampler = ClockSampler(physical_gpu_index(0))
+    sampler.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    count = 0
+    t0 = time.time()
+    s.record()
+    while time.time() - t0 < 4.0:
+        for _ in range(20):
+            fn()
+        count += 20
+        torch.cuda.synchronize()
+    e.record()
+    e.synchronize()
+    clocks = sampler.stop()
+    out = {
+        "tflops": flops / best / 1e9,
+        "tflops_sustained": flops * count / s.elapsed_time(e) / 1e9,
+        "how": "cuBLASLt MXFP8 via torch._scaled_mm, 8192^3, E4M3 x E4M3 with E8M0 1x32 scales -> BF16: "
+               "best of 10 (burst) and back to back for 4 s (sustained)",
+        "clocks_sustained": clocks,
+        "gpu": torch.cuda.get_device_name(0),
+    }
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.measure_fp8_peak:
+        measure_fp8_peak(args)
+        return
     if args.impl == "reference":
         bench_reference(args)
     else:

@@ -137,6 +137,38 @@ def dense_gemm(a, b, sfa, sfb, out, stream=None, config: GemmConfig | None = Non
     return out
 
 
+class PreparedGemm:
+    """A GEMM launch with every argument resolved once: calling it is a single C-ABI call.
+
+    Validation, plan resolution and workspace selection happen at construction,
+    so the call itself is cheap and safe to capture into a CUDA graph (the
+    library encodes the TMA descriptors into the kernel's parameters).
+    """
+
+    def __init__(self, a, b, sfa, sfb, out, stream=None, config: GemmConfig | None = None, workspace=None):
+        m, k = a.shape
+        n = b.shape[0]
+        # Full validation and a first launch-ready check through the public wrapper's rules.
+        self.config = config or GemmConfig()
+        self.handle = _stream_handle(stream)
+        self.plan = query(m, n, k, self.config)
+        if workspace is None and self.plan["workspace_bytes"] > 0:
+            workspace = workspace_for(a.device, self.handle, self.plan["workspace_bytes"])
+        self.workspace = workspace
+        self._tensors = (a, b, sfa, sfb, out)
+        self._cfg = self.config.to_c()
+        ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel())
+        self._args = (a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), out.data_ptr(), m, n, k,
+                      out.stride(0), ctypes.byref(self._cfg), ws_ptr, ws_bytes, self.handle)
+        self._fn = _lib.load().cutex_mxfp8_gemm
+        dense_gemm(a, b, sfa, sfb, out, stream=self.handle, config=self.config, workspace=workspace)
+
+    def __call__(self) -> None:
+        status = self._fn(*self._args)
+        if status != 0:
+            _lib.check(status, "cutex_mxfp8_gemm")
+
+
 def dense_gemm_v13(a_ptr: int, b_ptr: int, sfa_ptr: int, sfb_ptr: int, c_ptr: int,
                    max_active_clusters: int = 0, stream=None) -> None:
     """The reference's fixed M=N=K=16384 five-pointer launch, on the 2-CTA kernel."""
@@ -192,6 +224,7 @@ def mxfp8_gemm_launch(a, b, sfa, sfb, out, m, n, k, target, stream=None, *, kern
 __all__ = [
     "GEMM_CONFIGS",
     "GemmConfig",
+    "PreparedGemm",
     "dense_gemm",
     "dense_gemm_v13",
     "device_target",
