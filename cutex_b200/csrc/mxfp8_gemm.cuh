@@ -26,8 +26,8 @@
 //
 // K-stage: 128 K values. A stage holds the A tile (128 x 128 B), this CTA's B
 // rows (kTileN/kCtaGroup x 128 B), the 512-byte SFA chunk and the full SFB
-// chunk(s) of the MMA's N (each CTA of a pair loads its own copy; no
-// cluster-multicast loads are used anywhere).
+// chunk(s) of the MMA's N (each CTA of a pair loads its own copy; no load is
+// broadcast to several CTAs).
 #pragma once
 
 #include <cuda_bf16.h>
