@@ -54,6 +54,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--config", type=str, default="", help="native config as JSON, e.g. '{\"kernel\": 2}'")
     p.add_argument("--no-graph", action="store_true", help="plain launches instead of one CUDA graph")
+    p.add_argument("--sustained-s", type=float, default=2.0,
+                   help="also run the launches back to back for this many seconds (0: skip)")
     p.add_argument("--measure-fp8-peak", action="store_true",
                    help="measure cuBLASLt MXFP8 (torch._scaled_mm) 8192^3: best-of-10 burst and 4 s sustained")
     p.add_argument("--dist", choices=("square", "llm"), default="square",
@@ -375,6 +377,34 @@ def bench_cutex(args):
     if _lib.load().cutex_last_device_status(stream.cuda_stream) != 0:
         raise RuntimeError("device-side timeout in the timed region")
     elapsed_ms = start.elapsed_time(end)
+
+    # Sustained rate: the same launches back to back for ~args.sustained_s seconds
+    # (power-capped steady state on a 1 kW part), reported beside the timed value.
+    sustained = None
+    if args.sustained_s > 0:
+        sampler2 = ClockSampler(physical_gpu_index(local))
+        sampler2.start()
+        s4, e4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches = 0
+        t_wall = time.time()
+        with torch.cuda.stream(stream):
+            s4.record(stream)
+            while time.time() - t_wall < args.sustained_s:
+                if graph is not None:
+                    graph.replay()
+                else:
+                    for _ in range(args.steps):
+                        step()
+                launches += args.steps
+                stream.synchronize()
+            e4.record(stream)
+        torch.cuda.synchronize()
+        clocks2 = sampler2.stop()
+        ts = torch.tensor([s4.elapsed_time(e4)], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+        sustained = {"value": 2.0 * m * n * k * launches / (float(ts[0]) / 1e3) / 1e12, "unit": "TFLOP/s",
+                     "launches": launches, "seconds": float(ts[0]) / 1e3, "clocks": clocks2}
     # Back-to-back launches in one graph: the average launch duration is the
     # timed interval over the launch count (inter-kernel gaps included).
     t = torch.tensor([elapsed_ms, elapsed_ms / args.steps], dtype=torch.float64, device=device)
@@ -520,6 +550,7 @@ def bench_cutex(args):
             "e2e": e2e,
             "gpu_launches": args.steps,
             "clocks": clocks,
+            "sustained": sustained,
         }
         if allgather is not None:
             line["allgather"] = allgather

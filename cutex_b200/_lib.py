@@ -20,6 +20,7 @@ CUTEX_ERR_UNSUPPORTED_DEVICE = 4
 CUTEX_ERR_CUDA = 5
 CUTEX_ERR_TIMEOUT = 6
 CUTEX_ERR_WORKSPACE = 7
+CUTEX_ERR_DEVICE_CHECK = 8
 
 KERNEL_AUTO = 0
 KERNEL_1CTA = 1
@@ -38,7 +39,8 @@ class GemmConfigC(ctypes.Structure):
         ("max_ctas", ctypes.c_int32),
         ("epi_buffers", ctypes.c_int32),
         ("sf_buffers", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 7),
+        ("scheduler", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 6),
     ]
 
 
@@ -57,7 +59,7 @@ class GemmInfoC(ctypes.Structure):
         ("epi_buffers", ctypes.c_int32),
         ("raster_group", ctypes.c_int32),
         ("sf_buffers", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("scheduler", ctypes.c_int32),
         ("workspace_bytes", ctypes.c_int64),
     ]
 

@@ -117,7 +117,7 @@ using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CU
                           GemmArgs);
 
 struct Variant {
-  int cta_group, tile_n, stages, epi_bufs, sf_bufs, smem_bytes;
+  int cta_group, tile_n, stages, epi_bufs, sf_bufs, dynamic, smem_bytes;
   const void* fn;
   const void* fn_trace;  // instrumented twin (cutex_mxfp8_gemm_trace), or null
   bool attr_set_trace[kMaxDevices];
@@ -125,7 +125,7 @@ struct Variant {
   int max_clusters[kMaxDevices];
 };
 
-template <int CG, int BN, int S, int E, int F, bool T = false>
+template <int CG, int BN, int S, int E, int F, bool D, bool T = false>
 Variant make_variant() {
   Variant v{};
   v.cta_group = CG;
@@ -133,30 +133,45 @@ Variant make_variant() {
   v.stages = S;
   v.epi_bufs = E;
   v.sf_bufs = F;
+  v.dynamic = D ? 1 : 0;
   v.smem_bytes = GemmCfg<CG, BN, S, E, F>::kSmemBytes;
-  v.fn = reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F>);
-  v.fn_trace = T ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, true>) : nullptr;
+  v.fn = reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D>);
+  v.fn_trace = T ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, true>) : nullptr;
   return v;
 }
 
-// Instantiated kernels: (cta group, tile_n, stages, epilogue buffers, SF buffers).
+// Instantiated kernels: (cta group, tile_n, stages, epilogue buffers, SF buffers,
+// dynamic CLC scheduler, [instrumented twin]).
 Variant g_variants[] = {
-    make_variant<1, 128, 4, 2, 2>(), make_variant<1, 128, 5, 2, 2>(), make_variant<1, 128, 6, 1, 2>(),
-    make_variant<1, 128, 6, 1, 1>(), make_variant<1, 256, 3, 2, 2>(), make_variant<1, 256, 4, 1, 2>(),
-    make_variant<1, 256, 4, 1, 1, true>(), make_variant<2, 256, 4, 2, 2>(), make_variant<2, 256, 5, 2, 2>(),
-    make_variant<2, 256, 6, 1, 2>(), make_variant<2, 256, 6, 1, 1, true>(), make_variant<2, 256, 6, 1, 4>(),
-    make_variant<2, 256, 5, 2, 1, true>(), make_variant<2, 256, 5, 2, 4>(),
+    // dynamic (cluster launch control) scheduling: the default
+    make_variant<2, 256, 6, 1, 1, true, true>(), make_variant<2, 256, 5, 2, 1, true>(),
+    make_variant<2, 256, 6, 1, 2, true>(), make_variant<2, 256, 4, 2, 1, true>(),
+    make_variant<2, 128, 6, 2, 1, true>(), make_variant<2, 128, 8, 1, 1, true>(),
+    make_variant<1, 256, 4, 1, 1, true, true>(), make_variant<1, 256, 3, 2, 1, true>(),
+    make_variant<1, 128, 6, 1, 1, true>(), make_variant<1, 128, 5, 2, 1, true>(),
+    // static persistent scheduling
+    make_variant<1, 128, 4, 2, 2, false>(), make_variant<1, 128, 5, 2, 2, false>(),
+    make_variant<1, 128, 6, 1, 2, false>(), make_variant<1, 128, 6, 1, 1, false>(),
+    make_variant<1, 256, 3, 2, 2, false>(), make_variant<1, 256, 4, 1, 2, false>(),
+    make_variant<1, 256, 4, 1, 1, false, true>(), make_variant<2, 256, 4, 2, 2, false>(),
+    make_variant<2, 256, 5, 2, 2, false>(), make_variant<2, 256, 6, 1, 2, false>(),
+    make_variant<2, 256, 6, 1, 1, false, true>(), make_variant<2, 256, 6, 1, 4, false>(),
+    make_variant<2, 256, 5, 2, 1, false, true>(), make_variant<2, 256, 5, 2, 4, false>(),
 };
 
-Variant* find_variant(int cg, int bn, int stages, int epi, int sfb) {
+Variant* find_variant(int cg, int bn, int stages, int epi, int sfb, int dynamic) {
   Variant* best = nullptr;
   for (auto& v : g_variants) {
-    if (v.cta_group != cg || v.tile_n != bn) continue;
+    if (v.cta_group != cg || v.tile_n != bn || v.dynamic != dynamic) continue;
     if (stages != 0 && v.stages != stages) continue;
     if (epi != 0 && v.epi_bufs != epi) continue;
     if (sfb != 0 && v.sf_bufs != sfb) continue;
-    // Default: deepest ring, then two SF buffers, then the most epilogue buffers.
-    auto rank = [](const Variant& x) { return x.stages * 100 + (x.sf_bufs == 2 ? 10 : 0) + x.epi_bufs; };
+    // Default (measured, burst, 2-CTA 256x256): 5 stages + 2 epilogue buffers + 1 SF
+    // buffer, then the deepest ring with one SF buffer.
+    auto rank = [](const Variant& x) {
+      const bool preferred = x.cta_group == 2 && x.tile_n == 256 && x.stages == 5 && x.epi_bufs == 2;
+      return (preferred && x.sf_bufs == 1 ? 10000 : 0) + x.stages * 100 + (x.sf_bufs == 1 ? 10 : 0) - x.epi_bufs;
+    };
     if (best == nullptr || rank(v) > rank(*best)) best = &v;
   }
   return best;
@@ -235,7 +250,7 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   }
   if (cfg.kernel < 0 || cfg.kernel > CUTEX_KERNEL_SKINNY || cfg.stages < 0 || cfg.raster_group < 0 ||
       cfg.max_ctas < 0 || cfg.split_k < 0 || cfg.epi_buffers < 0 || cfg.epi_buffers > 2 ||
-      cfg.sf_buffers < 0 || cfg.sf_buffers > 4 ||
+      cfg.sf_buffers < 0 || cfg.sf_buffers > 4 || cfg.scheduler < 0 || cfg.scheduler > 1 ||
       (cfg.raster_along_n != 0 && cfg.raster_along_n != 1))
     return CUTEX_ERR_INVALID_ARGUMENT;
   if (cfg.tile_n != 0 && cfg.tile_n != 128 && cfg.tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
@@ -278,13 +293,16 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   }
   int tile_n = cfg.tile_n;
   if (kernel == CUTEX_KERNEL_2CTA) {
+    // 256x256 pair tiles. The 256x128 pair tile exists as an explicit option only:
+    // measured, it halves the B bytes per tile but starves the per-SM operand feed
+    // and runs at ~60 % of the 256x256 rate at 4096^3..16384^3.
     if (tile_n == 0) tile_n = 256;
-    if (tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
   } else if (tile_n == 0) {
     tile_n = (N % 256 == 0 && M > 128) ? 256 : 128;
   }
   const int cg = kernel == CUTEX_KERNEL_2CTA ? 2 : 1;
-  Variant* v = find_variant(cg, tile_n, cfg.stages, cfg.epi_buffers, cfg.sf_buffers);
+  Variant* v = find_variant(cg, tile_n, cfg.stages, cfg.epi_buffers, cfg.sf_buffers,
+                            cfg.scheduler == 1 ? 0 : 1);
   if (v == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
   plan->variant = v;
   plan->kernel = kernel;
@@ -296,6 +314,11 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   plan->num_tiles = static_cast<int>(tiles);
   plan->raster_group = cfg.raster_group != 0 ? cfg.raster_group : 8;
   plan->raster_along_n = cfg.raster_along_n;
+  if (v->dynamic) {
+    // One cluster per tile; resident clusters cancel and take over pending ones.
+    plan->grid_ctas = plan->num_tiles * cg;
+    return CUTEX_OK;
+  }
   int units = sm_count / cg;  // persistent CTAs (pairs) that fit, one per SM
   if (cfg.max_ctas != 0) units = std::min(units, std::max(1, cfg.max_ctas / cg));
   units = std::max(1, std::min(units, plan->num_tiles));
@@ -340,7 +363,7 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
 
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(static_cast<unsigned>(plan.grid_ctas), 1, 1);
-  lc.blockDim = dim3(192, 1, 1);
+  lc.blockDim = dim3(v->dynamic ? 224 : 192, 1, 1);
   lc.dynamicSmemBytes = static_cast<size_t>(v->smem_bytes);
   lc.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -365,7 +388,8 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
       std::lock_guard<std::mutex> lock(g_mutex);
       v->max_clusters[dev] = max_clusters;
     }
-    if (plan.grid_ctas > 2 * max_clusters) lc.gridDim.x = static_cast<unsigned>(2 * max_clusters);
+    if (!v->dynamic && plan.grid_ctas > 2 * max_clusters)
+      lc.gridDim.x = static_cast<unsigned>(2 * max_clusters);
   }
   void* params[] = {&ta, &tb, &tsa, &tsb, &td, &args};
   if (cudaLaunchKernelExC(&lc, fn, params) != cudaSuccess) return CUTEX_ERR_CUDA;
@@ -454,6 +478,7 @@ extern "C" int cutex_mxfp8_query(const cutex_gemm_config* cfg, int64_t M, int64_
   info->split_k = 1;
   info->epi_buffers = plan.variant->epi_bufs;
   info->sf_buffers = plan.variant->sf_bufs;
+  info->scheduler = plan.variant->dynamic ? 0 : 1;
   info->workspace_bytes = 0;
   return CUTEX_OK;
 }
@@ -560,6 +585,7 @@ extern "C" const char* cutex_status_string(int status) {
     case CUTEX_ERR_CUDA: return "CUTEX_ERR_CUDA: CUDA runtime or driver call failed";
     case CUTEX_ERR_TIMEOUT: return "CUTEX_ERR_TIMEOUT: device-side wait exceeded its limit";
     case CUTEX_ERR_WORKSPACE: return "CUTEX_ERR_WORKSPACE: workspace missing or too small";
+    case CUTEX_ERR_DEVICE_CHECK: return "CUTEX_ERR_DEVICE_CHECK: a device-side consistency check failed";
     default: return "CUTEX_ERR_UNKNOWN";
   }
 }
@@ -574,7 +600,7 @@ extern "C" int cutex_last_device_status(cutex_stream_t stream) {
     const int zero = 0;
     if (cudaMemcpyToSymbol(g_cutex_device_status, &zero, sizeof(int)) != cudaSuccess)
       return CUTEX_ERR_CUDA;
-    return CUTEX_ERR_TIMEOUT;
+    return value >= 0x200 ? CUTEX_ERR_DEVICE_CHECK : CUTEX_ERR_TIMEOUT;
   }
   return CUTEX_OK;
 }

@@ -46,6 +46,8 @@ enum DeviceError : int {
   kDevTimeoutMma = 0x102,
   kDevTimeoutEpilogue = 0x103,
   kDevTimeoutAccEmpty = 0x104,
+  kDevTimeoutScheduler = 0x105,
+  kDevBadTile = 0x201,  // a scheduled tile id outside [0, num_tiles): work stopped, nothing accessed
 };
 
 struct GemmArgs {
@@ -111,6 +113,16 @@ struct Tracer {
   }
 };
 
+// Traced builds also record every CTA's [start, end] globaltimer after the six
+// role regions: trace[6 * (trace_cap + 1) * 2 + 2 * blockIdx.x + {0, 1}].
+template <bool kOn>
+__device__ __forceinline__ void trace_cta_time(const GemmArgs& a, int which) {
+  if constexpr (kOn) {
+    if (a.trace != nullptr)
+      a.trace[static_cast<size_t>(6) * (a.trace_cap + 1) * 2 + 2 * blockIdx.x + which] = ptx::globaltimer();
+  }
+}
+
 constexpr int kSmemLimit = 232448;  // max dynamic shared memory per block on sm_100
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -135,9 +147,13 @@ struct GemmCfg {
   static constexpr int kOffC = align_up(kOffSFB + kStages * kSFBBytes, 1024);
   static constexpr int kCBufBytes = 32 * 64 * 2;  // 32 rows x 64 bf16, 128B-swizzled
   static constexpr int kOffBar = kOffC + 4 * kEpiBufs * kCBufBytes;
-  static constexpr int kNumBars = 2 * kStages + 4;
-  static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
-  static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + base alignment slack
+  // full[S], empty[S], acc_full[2], acc_empty[2], work_full[2], work_empty[2], clc
+  static constexpr int kNumBars = 2 * kStages + 9;
+  static constexpr int kOffMisc = align_up(kOffBar + kNumBars * 8, 16);
+  static constexpr int kOffTmemSlot = kOffMisc;       // TMEM base address from tcgen05.alloc
+  static constexpr int kOffWorkSlot = kOffMisc + 16;  // two tile ids of the work ring
+  static constexpr int kOffClcResp = kOffMisc + 32;   // 16-byte try_cancel response
+  static constexpr int kSmemBytes = kOffMisc + 48 + 1024;  // + base alignment slack
 
   static constexpr int kTmemCols = 512;
   static constexpr int kSFACols = 4;
@@ -158,7 +174,6 @@ struct GemmCfg {
 
   static_assert(kCtaGroup == 1 || kCtaGroup == 2, "cta group");
   static_assert(kTileN == 128 || kTileN == 256, "tile_n");
-  static_assert(kCtaGroup == 1 || kTileN == 256, "the CTA-pair kernel uses tile_n = 256");
   static_assert(kSFACols + kSFBCols <= kSFBufCols, "scale-factor columns");
   static_assert(kSFBufs == 1 || kSFBufs == 2 || kSFBufs == 4, "scale-factor buffers");
   static_assert(kSFACol + kSFReserved <= kTmemCols, "TMEM plan");
@@ -201,6 +216,60 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
+// Where each role gets its next output tile.
+//  static (kDynamic = false): tiles cluster_id, cluster_id + num_clusters, ...
+//  dynamic: a two-slot ring in shared memory filled by the pair leader's
+//  scheduler warp (the cluster's own tile first, then tiles of clusters it
+//  cancelled through cluster launch control); a negative id ends the walk.
+//  Every consumer reads the slot and then releases it on the leader's
+//  work_empty barrier (peer CTAs arrive remotely), so the scheduler never
+//  overwrites an id before all eleven (pair) or six (single CTA) consumers have
+//  read it.
+template <bool kDynamic, bool kPair>
+struct TileSource {
+  int t = 0, step = 1, num_tiles = 0;
+  uint32_t w = 0, full0 = 0, empty0 = 0, slot0 = 0;
+  bool peer = false;
+
+  __device__ __forceinline__ void init(int first, int stride, int tiles, uint32_t full_bar0,
+                                      uint32_t empty_bar0, uint32_t slot_addr0, bool is_peer) {
+    t = first;
+    step = stride;
+    num_tiles = tiles;
+    full0 = full_bar0;
+    empty0 = empty_bar0;
+    slot0 = slot_addr0;
+    peer = is_peer;
+  }
+
+  // Called by the consuming threads of a role: one thread (producer, MMA issuer)
+  // or all lanes of a warp (epilogue, whole_warp = true, which syncs the warp
+  // so every lane has read the slot before `releaser` frees it).
+  __device__ __forceinline__ bool next(int& tile, bool releaser, bool whole_warp, int* status) {
+    if constexpr (!kDynamic) {
+      if (t >= num_tiles) return false;
+      tile = t;
+      t += step;
+      return true;
+    } else {
+      const uint32_t s = w & 1u;
+      if (!ptx::mbar_wait<true>(full0 + 8u * s, (w >> 1) & 1u, status, kDevTimeoutScheduler)) return false;
+      tile = static_cast<int>(ptx::ld_shared_u32(slot0 + 4u * s));
+      if (tile >= num_tiles) {  // never act on an id outside the grid's tiles
+        atomicCAS(status, 0, kDevBadTile);
+        tile = -1;
+      }
+      if (whole_warp) __syncwarp();
+      if (releaser) {
+        if (kPair && peer) ptx::mbar_arrive_cluster(ptx::mapa(empty0 + 8u * s, 0));
+        else ptx::mbar_arrive(empty0 + 8u * s);
+      }
+      ++w;
+      return tile >= 0;
+    }
+  }
+};
+
 // Wait ~50 us so that TMA loads already in flight land before the CTA exits on
 // an error path (loads of valid addresses complete on their own).
 __device__ __forceinline__ void settle_inflight_copies() {
@@ -208,8 +277,9 @@ __device__ __forceinline__ void settle_inflight_copies() {
   while (ptx::globaltimer() - t0 < 50000ull) __nanosleep(1000);
 }
 
-template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs, int kSFBufs, bool kTrace = false>
-__global__ void __launch_bounds__(192, 1)
+template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs, int kSFBufs, bool kDynamic,
+          bool kTrace = false>
+__global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
     mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_sfa,
@@ -236,6 +306,10 @@ __global__ void __launch_bounds__(192, 1)
   auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
   auto acc_full_bar = [&](int b) { return bar0 + 8u * (2 * kStages + b); };
   auto acc_empty_bar = [&](int b) { return bar0 + 8u * (2 * kStages + 2 + b); };
+  const uint32_t work_full0 = bar0 + 8u * (2 * kStages + 4);
+  const uint32_t work_empty0 = bar0 + 8u * (2 * kStages + 6);
+  const uint32_t clc_bar = bar0 + 8u * (2 * kStages + 8);
+  const uint32_t work_slot0 = smem + C::kOffWorkSlot;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem_ptr + C::kOffTmemSlot);
 
   if (warp == 5 && lane == 0) {
@@ -251,7 +325,11 @@ __global__ void __launch_bounds__(192, 1)
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(acc_full_bar(b), 1);
       ptx::mbar_init(acc_empty_bar(b), 4 * kCtaGroup);
+      ptx::mbar_init(work_full0 + 8u * b, 1);
+      // producer + epilogue warps of every CTA, + the leader's MMA issuer
+      ptx::mbar_init(work_empty0 + 8u * b, 5 * kCtaGroup + 1);
     }
+    ptx::mbar_init(clc_bar, 1);
     ptx::fence_mbar_init();
   }
   if (warp == 4) {
@@ -263,6 +341,50 @@ __global__ void __launch_bounds__(192, 1)
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   Tracer<kTrace> tr;
+  if (threadIdx.x == 0) trace_cta_time<kTrace>(args, 0);
+  TileSource<kDynamic, kPair> src;
+  src.init(cluster_id, num_clusters, args.num_tiles, work_full0, work_empty0, work_slot0, !leader);
+  int t = 0;
+
+  if constexpr (kDynamic) {
+    if (warp == 6) {
+      // -------------------------------------------------------- tile scheduler
+      if (leader && lane == 0) {
+        int tile = cluster_id;
+        uint32_t clc_phase = 0;
+        const uint32_t resp = smem + C::kOffClcResp;
+        for (uint32_t w = 0;; ++w) {
+          const uint32_t s = w & 1u;
+          if (!ptx::mbar_wait<kPair>(work_empty0 + 8u * s, ((w >> 1) & 1u) ^ 1u, status,
+                                     kDevTimeoutScheduler))
+            break;
+          ptx::st_shared_u32(work_slot0 + 4u * s, static_cast<uint32_t>(tile));
+          ptx::mbar_arrive(work_full0 + 8u * s);
+          if constexpr (kPair) {
+            ptx::st_shared_cluster_u32(ptx::mapa(work_slot0 + 4u * s, 1), static_cast<uint32_t>(tile));
+            ptx::mbar_arrive_cluster(ptx::mapa(work_full0 + 8u * s, 1));
+          }
+          if (tile < 0) break;
+          // Steal the next not-yet-started cluster's tile (or learn there is none).
+          ptx::mbar_arrive_expect_tx(clc_bar, 16);
+          ptx::clc_try_cancel(resp, clc_bar);
+          if (!ptx::mbar_wait(clc_bar, clc_phase, status, kDevTimeoutScheduler)) {
+            tile = -1;  // publish the end marker so every role leaves its loop
+            continue;
+          }
+          clc_phase ^= 1u;
+          uint32_t first_x = 0;
+          tile = ptx::clc_query(resp, first_x) ? static_cast<int>(first_x / kCtaGroup) : -1;
+          if (tile >= 0 && (first_x >= gridDim.x || first_x % kCtaGroup != 0 || tile >= args.num_tiles)) {
+            atomicCAS(status, 0, kDevBadTile);  // inconsistent response: stop scheduling
+            tile = -1;
+          }
+          ptx::fence_proxy_async_smem();  // the response buffer is rewritten by the next request
+        }
+      }
+      __syncwarp();
+    }
+  }
 
   if (warp == 5) {
     // ------------------------------------------------------------ TMA producer
@@ -271,7 +393,7 @@ __global__ void __launch_bounds__(192, 1)
       tr.rec(kEvStart, 0, 0);
       uint32_t kit = 0;
       bool ok = true;
-      for (int t = cluster_id; ok && t < args.num_tiles; t += num_clusters) {
+      while (ok && src.next(t, true, false, status)) {
         int mt, nt;
         tile_coords(t, args, mt, nt);
         const int a_row = mt * (128 * kCtaGroup) + static_cast<int>(rank) * 128;
@@ -328,7 +450,7 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t kit = 0;
       bool ok = true;
       int it = 0;
-      for (int t = cluster_id; ok && t < args.num_tiles; t += num_clusters, ++it) {
+      for (; ok && src.next(t, true, false, status); ++it) {
         const int buf = it & 1;
         tr.rec(kEvMmaAccWait, t, 0);
         if constexpr (C::kOverlap) {
@@ -388,14 +510,15 @@ __global__ void __launch_bounds__(192, 1)
       tr.close();
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------ epilogue
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ epilogue (warps 0-3 only;
+    // warp 6, the scheduler of the dynamic build, has no TMEM lane quarter)
     const uint32_t cbuf = smem + C::kOffC + warp * kEpiBufs * C::kCBufBytes;
     uint32_t chunk_ctr = 0;
     int it = 0;
     if (warp == 0 && lane == 0) tr.open(args, cluster_id == 0, static_cast<int>(rank) * 3 + 2);
     tr.rec(kEvStart, 0, 0);
-    for (int t = cluster_id; t < args.num_tiles; t += num_clusters, ++it) {
+    for (; src.next(t, lane == 0, true, status); ++it) {
       int mt, nt;
       tile_coords(t, args, mt, nt);
       const int m_row = mt * (128 * kCtaGroup) + static_cast<int>(rank) * 128 + warp * 32;
@@ -457,6 +580,7 @@ __global__ void __launch_bounds__(192, 1)
   // ------------------------------------------------------------ teardown
   ptx::tc_fence_before();
   if constexpr (kPair) ptx::cluster_sync(); else __syncthreads();
+  if (threadIdx.x == 0) trace_cta_time<kTrace>(args, 1);
   if (warp == 4) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc<kCtaGroup>(tmem_base, C::kTmemCols);

@@ -208,6 +208,50 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
+// ---------------------------------------------------------------- cluster launch control
+
+// Ask the hardware to cancel a cluster of this grid that has not started yet;
+// the 16-byte response lands in this CTA's shared memory at `resp` and
+// completes 16 bytes of transaction count on `bar`.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+          resp),
+      "r"(bar)
+      : "memory");
+}
+
+// Decode a try_cancel response: true and the x index of the cancelled
+// cluster's first CTA if a cluster was cancelled, false if none was left.
+__device__ __forceinline__ bool clc_query(uint32_t resp, uint32_t& first_ctaid_x) {
+  uint32_t ok = 0, x = 0, y = 0, z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b128 r;\n\t"
+      "ld.shared.b128 r, [%4];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid.v4.b32.b128 {%1, %2, %3, _}, r;\n\t}"
+      : "=r"(ok), "=r"(x), "=r"(y), "=r"(z)
+      : "r"(resp)
+      : "memory");
+  first_ctaid_x = x;
+  return ok != 0;
+}
+
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 template <int kCtaGroup>

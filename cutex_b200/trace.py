@@ -58,6 +58,20 @@ class GemmTrace:
     capacity: int
     shape: tuple[int, int, int]
     config: dict[str, Any] = field(default_factory=dict)
+    cta_times: list[tuple[int, int]] = field(default_factory=list)  # (start_ns, end_ns) per CTA
+
+    def cta_spread(self) -> dict[str, float]:
+        """How unevenly the persistent CTAs finish: end-time spread relative to the kernel span."""
+
+        times = [(s, e) for s, e in self.cta_times if s and e]
+        if not times:
+            return {}
+        t0 = min(s for s, _ in times)
+        ends = sorted(e - t0 for _, e in times)
+        span = ends[-1]
+        return {"ctas": len(times), "span_us": span / 1e3, "first_end_us": ends[0] / 1e3,
+                "median_end_us": ends[len(ends) // 2] / 1e3,
+                "idle_fraction": sum(span - e for e in ends) / (span * len(ends)) if span else 0.0}
 
     def role_events(self, cta: int, role: str) -> list[Event]:
         return [e for e in self.events if e.cta == cta and e.role == role]
@@ -81,7 +95,8 @@ class GemmTrace:
     def summary(self) -> dict[str, Any]:
         """Per CTA and role: elapsed time and the total/mean of each wait span."""
 
-        result: dict[str, Any] = {"shape": list(self.shape), "config": self.config, "ctas": {}}
+        result: dict[str, Any] = {"shape": list(self.shape), "config": self.config, "ctas": {},
+                                  "cta_finish": self.cta_spread()}
         for cta in sorted({e.cta for e in self.events}):
             per_role = {}
             for role in ROLES:
@@ -156,10 +171,11 @@ def run_gemm_trace(a, b, sfa, sfb, out, config=None, capacity: int = 1 << 16) ->
 
     import torch
 
-    from .kernels.dense_gemm import GemmConfig, _stream_handle
+    from .kernels.dense_gemm import GemmConfig, _stream_handle, query
 
     cfg = config or GemmConfig(kernel=2, stages=6, epi_buffers=1, sf_buffers=1)
-    buf = torch.zeros(6 * (capacity + 1) * 2, dtype=torch.int64, device=out.device)
+    max_ctas = 1024
+    buf = torch.zeros(6 * (capacity + 1) * 2 + 2 * max_ctas, dtype=torch.int64, device=out.device)
     m, k = a.shape
     n = b.shape[0]
     status = _lib.load().cutex_mxfp8_gemm_trace(
@@ -171,7 +187,10 @@ def run_gemm_trace(a, b, sfa, sfb, out, config=None, capacity: int = 1 << 16) ->
     events = decode(raw, capacity)
     if not events:
         raise TraceError("the traced launch recorded no events")
-    return GemmTrace(events, capacity, (m, n, k), dict(cfg.__dict__))
+    base = 6 * (capacity + 1) * 2
+    grid = query(m, n, k, cfg)["grid_ctas"]
+    cta_times = [(int(raw[base + 2 * c]), int(raw[base + 2 * c + 1])) for c in range(min(grid, max_ctas))]
+    return GemmTrace(events, capacity, (m, n, k), dict(cfg.__dict__), cta_times)
 
 
 def disabled_trace_metadata() -> dict[str, Any]:

@@ -45,7 +45,8 @@ typedef enum cutex_status {
   CUTEX_ERR_UNSUPPORTED_DEVICE = 4, /* current device is not compute capability 10.0 */
   CUTEX_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed */
   CUTEX_ERR_TIMEOUT = 6,          /* a device-side bounded wait expired */
-  CUTEX_ERR_WORKSPACE = 7         /* workspace missing or smaller than required */
+  CUTEX_ERR_WORKSPACE = 7,        /* workspace missing or smaller than required */
+  CUTEX_ERR_DEVICE_CHECK = 8      /* a device-side consistency check stopped a kernel */
 } cutex_status;
 
 /* Kernel families. */
@@ -70,7 +71,9 @@ typedef struct cutex_gemm_config {
   int32_t max_ctas;       /* cap on persistent CTAs (0 = one per SM) */
   int32_t epi_buffers;    /* epilogue staging buffers per warp (1 or 2) */
   int32_t sf_buffers;     /* rotating scale-factor TMEM buffers (1, 2 or 4) */
-  int32_t reserved[7];    /* must be zero */
+  int32_t scheduler;      /* 0: dynamic (one cluster per tile, idle clusters take over pending
+                             ones through cluster launch control); 1: static persistent grid */
+  int32_t reserved[6];    /* must be zero */
 } cutex_gemm_config;
 
 /* What a launch with this configuration would do (filled by cutex_mxfp8_query). */
@@ -88,7 +91,7 @@ typedef struct cutex_gemm_info {
   int32_t epi_buffers;
   int32_t raster_group;
   int32_t sf_buffers;
-  int32_t reserved0;
+  int32_t scheduler;
   int64_t workspace_bytes; /* device workspace the GEMM call needs (0 for most shapes) */
 } cutex_gemm_info;
 
@@ -127,10 +130,11 @@ CUTEX_API int cutex_mxfp8_query(const cutex_gemm_config* cfg, int64_t M, int64_t
 /*
  * Diagnostics: the same GEMM on an instrumented build of the kernel that
  * records per-role %globaltimer events of the first CTA (pair) into `trace`
- * (caller-allocated, 8-byte aligned, 6 * (trace_cap + 1) * 2 uint64 values:
- * regions [cta_rank * 3 + role], role 0 = TMA producer, 1 = MMA issuer,
- * 2 = epilogue warp 0; record 0 of a region = event count, record i = {time_ns,
- * event << 56 | tile << 24 | k_block}). Only configurations with an
+ * (caller-allocated, 8-byte aligned, 6 * (trace_cap + 1) * 2 + 2 * grid_ctas
+ * uint64 values, grid_ctas from cutex_mxfp8_query: regions [cta_rank * 3 +
+ * role], role 0 = TMA producer, 1 = MMA issuer, 2 = epilogue warp 0; record 0
+ * of a region = event count, record i = {time_ns, event << 56 | tile << 24 |
+ * k_block}; then {start_ns, end_ns} of every CTA). Only configurations with an
  * instrumented twin are accepted (CUTEX_ERR_INVALID_ARGUMENT otherwise).
  * Replaces the reference's IKET in-kernel ranges (cutex/trace.py:96-175,
  * cutex/kernels/dense_gemm_v9.py:116-125); benchmark builds carry no tracing.
@@ -191,7 +195,7 @@ CUTEX_API const char* cutex_status_string(int status);
 /*
  * Synchronise `stream`, return the first device-side error recorded by a
  * kernel of this library on the current device since the last call
- * (CUTEX_OK or CUTEX_ERR_TIMEOUT), and clear it.
+ * (CUTEX_OK, CUTEX_ERR_TIMEOUT or CUTEX_ERR_DEVICE_CHECK), and clear it.
  */
 CUTEX_API int cutex_last_device_status(cutex_stream_t stream);
 

@@ -36,10 +36,11 @@ def test_library_exports_every_declared_symbol():
 def test_struct_layouts_match_header():
     assert ctypes.sizeof(_lib.GemmConfigC) == 16 * 4
     assert ctypes.sizeof(_lib.GemmInfoC) == 14 * 4 + 8
+    assert _lib.GemmInfoC.scheduler.offset == 13 * 4
 
 
 def test_status_strings():
-    for code in range(8):
+    for code in range(9):
         assert _lib.status_string(code).startswith("CUTEX_")
     assert "UNKNOWN" in _lib.status_string(99)
     assert _lib.version().startswith("cutex-b200")
@@ -80,8 +81,13 @@ def test_query_resolves_plans_without_launching():
     assert lib.cutex_mxfp8_query(ctypes.byref(cfg), C.M, C.N, C.K, ctypes.byref(info)) == 0
     assert info.kernel == _lib.KERNEL_2CTA and info.tile_m == 256 and info.tile_n == 256
     assert info.cluster_size == 2 and info.num_tiles == 64 * 64
-    assert info.smem_bytes <= 232448 and info.grid_ctas % 2 == 0
-    cfg = _lib.make_config(kernel=1, tile_n=128, stages=5)
+    assert info.smem_bytes <= 232448 and info.grid_ctas == 2 * 64 * 64 and info.scheduler == 0
+    static = _lib.make_config(scheduler=1)
+    assert lib.cutex_mxfp8_query(ctypes.byref(static), C.M, C.N, C.K, ctypes.byref(info)) == 0
+    assert info.scheduler == 1 and info.grid_ctas <= 148
+    bad = _lib.make_config(scheduler=2)
+    assert lib.cutex_mxfp8_query(ctypes.byref(bad), 256, 256, 256, ctypes.byref(info)) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    cfg = _lib.make_config(kernel=1, tile_n=128, stages=5, scheduler=1)
     assert lib.cutex_mxfp8_query(ctypes.byref(cfg), 300, 272, 384, ctypes.byref(info)) == 0
     assert (info.tile_m, info.tile_n, info.stages, info.num_tiles) == (128, 128, 5, 3 * 3)
     bad = _lib.make_config(tile_n=96)

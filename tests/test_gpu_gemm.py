@@ -13,32 +13,47 @@ from tests.gpu_helpers import GemmConfig, O, check, device_ok, make_operands, ru
 
 pytestmark = pytest.mark.gpu
 
+# Every instantiated kernel: dynamic (cluster launch control, scheduler=0) and static (scheduler=1).
 VARIANTS = [
-    GemmConfig(kernel=1, tile_n=128, stages=6, epi_buffers=1),
-    GemmConfig(kernel=1, tile_n=128, stages=5, epi_buffers=2),
-    GemmConfig(kernel=1, tile_n=128, stages=4, epi_buffers=2),
-    GemmConfig(kernel=1, tile_n=256, stages=4, epi_buffers=1),
-    GemmConfig(kernel=1, tile_n=256, stages=3, epi_buffers=2),
-    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1),
-    GemmConfig(kernel=2, tile_n=256, stages=5, epi_buffers=2),
-    GemmConfig(kernel=2, tile_n=256, stages=4, epi_buffers=2),
-    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1, sf_buffers=1),
-    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1, sf_buffers=4),
-    GemmConfig(kernel=2, tile_n=256, stages=5, epi_buffers=2, sf_buffers=4),
-    GemmConfig(kernel=1, tile_n=256, stages=4, epi_buffers=1, sf_buffers=1),
-    GemmConfig(kernel=1, tile_n=128, stages=6, epi_buffers=1, sf_buffers=1),
+    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1, sf_buffers=1, scheduler=0),
+    GemmConfig(kernel=2, tile_n=256, stages=5, epi_buffers=2, sf_buffers=1, scheduler=0),
+    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1, sf_buffers=2, scheduler=0),
+    GemmConfig(kernel=2, tile_n=256, stages=4, epi_buffers=2, sf_buffers=1, scheduler=0),
+    GemmConfig(kernel=1, tile_n=256, stages=4, epi_buffers=1, sf_buffers=1, scheduler=0),
+    GemmConfig(kernel=1, tile_n=256, stages=3, epi_buffers=2, sf_buffers=1, scheduler=0),
+    GemmConfig(kernel=1, tile_n=128, stages=6, epi_buffers=1, sf_buffers=1, scheduler=0),
+    GemmConfig(kernel=1, tile_n=128, stages=5, epi_buffers=2, sf_buffers=1, scheduler=0),
+    GemmConfig(kernel=1, tile_n=128, stages=6, epi_buffers=1, sf_buffers=2, scheduler=1),
+    GemmConfig(kernel=1, tile_n=128, stages=5, epi_buffers=2, sf_buffers=2, scheduler=1),
+    GemmConfig(kernel=1, tile_n=128, stages=4, epi_buffers=2, sf_buffers=2, scheduler=1),
+    GemmConfig(kernel=1, tile_n=128, stages=6, epi_buffers=1, sf_buffers=1, scheduler=1),
+    GemmConfig(kernel=1, tile_n=256, stages=4, epi_buffers=1, sf_buffers=2, scheduler=1),
+    GemmConfig(kernel=1, tile_n=256, stages=3, epi_buffers=2, sf_buffers=2, scheduler=1),
+    GemmConfig(kernel=1, tile_n=256, stages=4, epi_buffers=1, sf_buffers=1, scheduler=1),
+    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1, sf_buffers=2, scheduler=1),
+    GemmConfig(kernel=2, tile_n=256, stages=5, epi_buffers=2, sf_buffers=2, scheduler=1),
+    GemmConfig(kernel=2, tile_n=256, stages=4, epi_buffers=2, sf_buffers=2, scheduler=1),
+    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1, sf_buffers=1, scheduler=1),
+    GemmConfig(kernel=2, tile_n=256, stages=6, epi_buffers=1, sf_buffers=4, scheduler=1),
+    GemmConfig(kernel=2, tile_n=256, stages=5, epi_buffers=2, sf_buffers=4, scheduler=1),
+    GemmConfig(kernel=2, tile_n=256, stages=5, epi_buffers=2, sf_buffers=1, scheduler=1),
+    GemmConfig(kernel=2, tile_n=128, stages=6, epi_buffers=2, sf_buffers=1, scheduler=0),
+    GemmConfig(kernel=2, tile_n=128, stages=8, epi_buffers=1, sf_buffers=1, scheduler=0),
 ]
+DYN_2CTA, DYN_1CTA_256, DYN_1CTA_128 = VARIANTS[0], VARIANTS[4], VARIANTS[6]
+DYN_2CTA_128 = VARIANTS[23]
+ST_1CTA_128, ST_1CTA_256, ST_2CTA = VARIANTS[11], VARIANTS[14], VARIANTS[18]
 
 
 def _id(cfg):
-    return f"k{cfg.kernel}_n{cfg.tile_n}_s{cfg.stages}_e{cfg.epi_buffers}_f{cfg.sf_buffers}"
+    return f"k{cfg.kernel}_n{cfg.tile_n}_s{cfg.stages}_e{cfg.epi_buffers}_f{cfg.sf_buffers}_{'st' if cfg.scheduler else 'dyn'}"
 
 
 def _assert_ok(report):
     assert report["ok"], report
 
 
-@pytest.mark.parametrize("cfg", VARIANTS[:1] + VARIANTS[3:4] + VARIANTS[5:6], ids=_id)
+@pytest.mark.parametrize("cfg", [DYN_2CTA, DYN_1CTA_256, DYN_1CTA_128, ST_1CTA_128, ST_2CTA, DYN_2CTA_128], ids=_id)
 def test_single_tile(cfg):
     M, N, K = 128, 256, 128
     a, sfa, b, sfb = make_operands(M, N, K, seed=1)
@@ -53,7 +68,7 @@ def test_variants_square(cfg, shape):
     _assert_ok(check(run_gemm(a, sfa, b, sfb, M, N, K, cfg), a, sfa, b, sfb, M, N, K))
 
 
-@pytest.mark.parametrize("cfg", [VARIANTS[0], VARIANTS[3], VARIANTS[5]], ids=_id)
+@pytest.mark.parametrize("cfg", [DYN_2CTA, DYN_1CTA_128, ST_1CTA_256, ST_2CTA, DYN_2CTA_128], ids=_id)
 @pytest.mark.parametrize("shape", [(200, 272, 384), (1, 16, 128), (129, 48, 256), (300, 528, 640), (777, 1040, 512)],
                          ids=str)
 def test_ragged_shapes(cfg, shape):
@@ -62,7 +77,7 @@ def test_ragged_shapes(cfg, shape):
     _assert_ok(check(run_gemm(a, sfa, b, sfb, M, N, K, cfg), a, sfa, b, sfb, M, N, K))
 
 
-@pytest.mark.parametrize("cfg", [VARIANTS[0], VARIANTS[3], VARIANTS[5]], ids=_id)
+@pytest.mark.parametrize("cfg", [ST_1CTA_128, ST_1CTA_256, ST_2CTA], ids=_id)
 def test_many_tiles_per_cta(cfg):
     # Few persistent CTAs walk many tiles: exercises ring wrap across tiles and
     # both TMEM accumulator buffers (and their overlap) many times over.
@@ -72,12 +87,21 @@ def test_many_tiles_per_cta(cfg):
     _assert_ok(check(run_gemm(a, sfa, b, sfb, M, N, K, cfg), a, sfa, b, sfb, M, N, K))
 
 
-@pytest.mark.parametrize("cfg", [VARIANTS[0], VARIANTS[5]], ids=_id)
+@pytest.mark.parametrize("cfg", [DYN_2CTA, ST_1CTA_128, ST_2CTA], ids=_id)
 @pytest.mark.parametrize("raster", [(1, 0), (3, 1), (16, 0)], ids=str)
 def test_rasterisation_orders(cfg, raster):
     M, N, K = 768, 1280, 256
     a, sfa, b, sfb = make_operands(M, N, K, seed=5)
     cfg = GemmConfig(**{**cfg.__dict__, "raster_group": raster[0], "raster_along_n": raster[1]})
+    _assert_ok(check(run_gemm(a, sfa, b, sfb, M, N, K, cfg), a, sfa, b, sfb, M, N, K))
+
+
+@pytest.mark.parametrize("cfg", [DYN_2CTA, DYN_1CTA_256, DYN_1CTA_128, DYN_2CTA_128], ids=_id)
+def test_dynamic_scheduler_steals_pending_clusters(cfg):
+    # Far more tiles than resident clusters: most tiles are taken over from
+    # cancelled clusters through cluster launch control.
+    M, N, K = 4096, 4096, 256
+    a, sfa, b, sfb = make_operands(M, N, K, seed=29)
     _assert_ok(check(run_gemm(a, sfa, b, sfb, M, N, K, cfg), a, sfa, b, sfb, M, N, K))
 
 
@@ -107,7 +131,8 @@ def test_repeated_calls_are_deterministic():
     M, N, K = 512, 512, 2048
     a, sfa, b, sfb = make_operands(M, N, K, seed=17)
     first = run_gemm(a, sfa, b, sfb, M, N, K).clone()
-    for cfg in (GemmConfig(kernel=1, tile_n=128), GemmConfig(kernel=2)):
+    for cfg in (GemmConfig(kernel=1, tile_n=128), GemmConfig(kernel=2), GemmConfig(kernel=2, scheduler=1),
+                GemmConfig(kernel=1, tile_n=256, scheduler=1)):
         again = run_gemm(a, sfa, b, sfb, M, N, K, cfg)
         # Same K-order accumulation inside every MMA tile: bitwise identical across variants.
         assert torch.equal(first.view(torch.int16), again.view(torch.int16))

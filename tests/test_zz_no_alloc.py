@@ -17,7 +17,7 @@ import pytest
 import torch
 
 from cutex_b200 import _lib
-from cutex_b200.kernels import query
+from cutex_b200.kernels import GemmConfig, query
 from tests.gpu_helpers import O, check, device_ok, make_operands
 
 pytestmark = pytest.mark.gpu
@@ -25,7 +25,8 @@ pytestmark = pytest.mark.gpu
 
 def _regular(ta, tb, tsa, tsb, M, N, K):
     out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-    ws = torch.zeros(query(M, N, K)["workspace_bytes"], dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(query(M, N, K, GemmConfig(kernel=_lib.KERNEL_SKINNY))["workspace_bytes"], dtype=torch.uint8,
+                     device="cuda")
     cfg = _lib.make_config(kernel=_lib.KERNEL_SKINNY)
     rc = _lib.load().cutex_mxfp8_gemm(ta.data_ptr(), tb.data_ptr(), tsa.data_ptr(), tsb.data_ptr(), out.data_ptr(),
                                       M, N, K, N, ctypes.byref(cfg), ws.data_ptr(), ws.numel(),
