@@ -417,7 +417,7 @@ def bench_cutex(args):
     flops_launch = 2.0 * m * n_local * k
     bytes_launch = float(m * k + n_local * k + (m + n_local) * (k // 32) + 2 * m * n_local)
     peaks, source = load_peaks()
-    sustained = elapsed_ms > 2000.0
+    long_timed = elapsed_ms > 2000.0
     workload = workload_name(m, n, k)
     hbm_bound = flops_launch / bytes_launch < RIDGE_FLOP_PER_BYTE
     if hbm_bound:
@@ -425,7 +425,7 @@ def bench_cutex(args):
         peak, peak_src = float(peaks["hbm_gbs"]), f"{source} HBM copy (hbm_gbs)"
     else:
         achieved = flops_launch / (launch_avg_ms / 1e3) / 1e12
-        peak, peak_src = fp8_peak(peaks, source, sustained)
+        peak, peak_src = fp8_peak(peaks, source, long_timed)
 
     # ---- end to end through the C ABI with pinned host buffers
     e2e = None
