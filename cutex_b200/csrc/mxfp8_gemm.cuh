@@ -6,14 +6,16 @@
 // (128*kCtaGroup) x kTileN output tile at a time and walks a static,
 // grouped-raster sequence of tiles (persistent grid sized to the SM count).
 //
-// Warp roles (192 threads):
+// Warp roles (192 threads, 224 with the dynamic scheduler):
 //   warps 0-3  epilogue: TMEM -> registers -> BF16 -> swizzled SMEM -> TMA store.
 //              Warp w owns TMEM lanes [32w, 32w+32), i.e. output rows 32w..32w+31.
-//   warp 4     MMA issuer (one thread; the pair leader only when kCtaGroup = 2):
-//              per K-stage copies the SFA/SFB chunks SMEM->TMEM (tcgen05.cp) and
-//              issues four K=32 block-scaled MMAs, then commits the stage back.
-//   warp 5     TMA producer (one thread per CTA): A, B, SFA, SFB tiles into a
-//              kStages-deep ring guarded by full/empty mbarriers.
+//   warp 4     MMA issuer (the pair leader's warp when kCtaGroup = 2): the warp
+//              waits converged and one elected lane per K-stage copies the
+//              SFA/SFB chunks SMEM->TMEM (tcgen05.cp), issues four K=32
+//              block-scaled MMAs and commits the stage back.
+//   warp 5     TMA producer (every CTA; one elected lane issues): A, B, SFA, SFB
+//              tiles into a kStages-deep ring guarded by full/empty mbarriers.
+//   warp 6     tile scheduler (dynamic builds, pair leader): cluster launch control.
 //
 // TMEM plan (512 columns, 32-bit): two accumulator buffers alternate by tile.
 // When two full buffers plus the scale-factor columns do not fit (tile_n =
@@ -114,12 +116,18 @@ struct Tracer {
 };
 
 // Traced builds also record every CTA's [start, end] globaltimer after the six
-// role regions: trace[6 * (trace_cap + 1) * 2 + 2 * blockIdx.x + {0, 1}].
+// role regions, trace[6 * (trace_cap + 1) * 2 + 2 * blockIdx.x + {0, 1}], and the
+// SM cycle counter at the same two points after those, at + 2 * gridDim.x
+// (cycles over nanoseconds = the SM clock the CTA actually ran at).
 template <bool kOn>
 __device__ __forceinline__ void trace_cta_time(const GemmArgs& a, int which) {
   if constexpr (kOn) {
-    if (a.trace != nullptr)
-      a.trace[static_cast<size_t>(6) * (a.trace_cap + 1) * 2 + 2 * blockIdx.x + which] = ptx::globaltimer();
+    if (a.trace != nullptr) {
+      unsigned long long* base = a.trace + static_cast<size_t>(6) * (a.trace_cap + 1) * 2;
+      const unsigned long long clk = ptx::clock64();
+      base[2 * blockIdx.x + which] = ptx::globaltimer();
+      base[2 * gridDim.x + 2 * blockIdx.x + which] = clk;
+    }
   }
 }
 
@@ -253,7 +261,9 @@ struct TileSource {
       return true;
     } else {
       const uint32_t s = w & 1u;
-      if (!ptx::mbar_wait<true>(full0 + 8u * s, (w >> 1) & 1u, status, kDevTimeoutScheduler)) return false;
+      bool ok = ptx::mbar_wait<true>(full0 + 8u * s, (w >> 1) & 1u, status, kDevTimeoutScheduler);
+      if (whole_warp) ok = __all_sync(0xffffffffu, ok) != 0;
+      if (!ok) return false;
       tile = static_cast<int>(ptx::ld_shared_u32(slot0 + 4u * s));
       if (tile >= num_tiles) {  // never act on an id outside the grid's tiles
         atomicCAS(status, 0, kDevBadTile);
@@ -388,28 +398,30 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
 
   if (warp == 5) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      tr.open(args, cluster_id == 0, static_cast<int>(rank) * 3 + 0);
-      tr.rec(kEvStart, 0, 0);
-      uint32_t kit = 0;
-      bool ok = true;
-      while (ok && src.next(t, true, false, status)) {
-        int mt, nt;
-        tile_coords(t, args, mt, nt);
-        const int a_row = mt * (128 * kCtaGroup) + static_cast<int>(rank) * 128;
-        const int b_row = nt * kTileN + static_cast<int>(rank) * C::kLoadN;
-        const int sfa_blk = a_row / 128;
-        const int sfb_blk = (nt * kTileN) / 128;
-        const uint64_t pol = ptx::policy_evict_normal();
-        for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
-          const int s = static_cast<int>(kit % kStages);
-          const uint32_t round = kit / kStages;
-          tr.rec(kEvProdWait, t, kb);
-          if (!ptx::mbar_wait(empty_bar(s), (round & 1u) ^ 1u, status, kDevTimeoutProducer)) {
-            ok = false;
-            break;
-          }
-          tr.rec(kEvProdGo, t, kb);
+    // The whole warp walks the tiles and waits (converged); one elected lane
+    // issues the copies.
+    if (lane == 0) tr.open(args, cluster_id == 0, static_cast<int>(rank) * 3 + 0);
+    tr.rec(kEvStart, 0, 0);
+    uint32_t kit = 0;
+    bool ok = true;
+    while (ok && src.next(t, lane == 0, true, status)) {
+      int mt, nt;
+      tile_coords(t, args, mt, nt);
+      const int a_row = mt * (128 * kCtaGroup) + static_cast<int>(rank) * 128;
+      const int b_row = nt * kTileN + static_cast<int>(rank) * C::kLoadN;
+      const int sfa_blk = a_row / 128;
+      const int sfb_blk = (nt * kTileN) / 128;
+      for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
+        const int s = static_cast<int>(kit % kStages);
+        const uint32_t round = kit / kStages;
+        tr.rec(kEvProdWait, t, kb);
+        if (!ptx::mbar_wait_warp(empty_bar(s), (round & 1u) ^ 1u, status, kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        tr.rec(kEvProdGo, t, kb);
+        if (ptx::elect_one()) {
+          const uint64_t pol = ptx::policy_evict_normal();
           if (leader) ptx::mbar_arrive_expect_tx(full_bar(s), C::kTxBytes);
           const uint32_t sa = smem + C::kOffA + s * C::kABytes;
           const uint32_t sb = smem + C::kOffB + s * C::kBBytes;
@@ -430,37 +442,42 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
             ptx::tma_load_3d(ssfb, &tmap_sfb, fb, 0, kb, sfb_blk, pol);
           }
         }
+        __syncwarp();
       }
-      // Drain: every stage this CTA filled has been consumed by the MMAs.
-      for (int i = 0; ok && i < kStages; ++i) {
-        const uint32_t k2 = kit + i;
-        ok = ptx::mbar_wait(empty_bar(static_cast<int>(k2 % kStages)),
-                            ((k2 / kStages) & 1u) ^ 1u, status, kDevTimeoutProducer);
-      }
-      if (!ok) settle_inflight_copies();
-      tr.rec(kEvEnd, 0, 0);
-      tr.close();
     }
-    __syncwarp();
+    // Drain: every stage this CTA filled has been consumed by the MMAs.
+    for (int i = 0; ok && i < kStages; ++i) {
+      const uint32_t k2 = kit + i;
+      ok = ptx::mbar_wait_warp(empty_bar(static_cast<int>(k2 % kStages)), ((k2 / kStages) & 1u) ^ 1u, status,
+                               kDevTimeoutProducer);
+    }
+    if (!ok) settle_inflight_copies();
+    tr.rec(kEvEnd, 0, 0);
+    tr.close();
   } else if (warp == 4) {
     // ------------------------------------------------------------ MMA issuer
-    if (leader && lane == 0) {
-      tr.open(args, cluster_id == 0, 1);
+    // The whole warp walks the tiles and waits (converged); one elected lane
+    // issues the tcgen05 operations. Issued from a lone-lane branch instead,
+    // the SMEM->TMEM scale copies and the MMAs stop overlapping once the tensor
+    // pipe has run empty (a wait at a tile boundary or for data), which cost
+    // ~15 % of the tensor pipe.
+    if (leader) {
+      if (lane == 0) tr.open(args, cluster_id == 0, 1);
       tr.rec(kEvStart, 0, 0);
       uint32_t kit = 0;
       bool ok = true;
       int it = 0;
-      for (; ok && src.next(t, true, false, status); ++it) {
+      for (; ok && src.next(t, lane == 0, true, status); ++it) {
         const int buf = it & 1;
         tr.rec(kEvMmaAccWait, t, 0);
         if constexpr (C::kOverlap) {
           if (it >= 1)
-            ok = ptx::mbar_wait<kPair>(acc_empty_bar((it - 1) & 1), ((it - 1) >> 1) & 1, status,
-                                       kDevTimeoutAccEmpty);
+            ok = ptx::mbar_wait_warp<kPair>(acc_empty_bar((it - 1) & 1), ((it - 1) >> 1) & 1, status,
+                                            kDevTimeoutAccEmpty);
         } else {
           if (it >= 2)
-            ok = ptx::mbar_wait<kPair>(acc_empty_bar(buf), ((it - 2) >> 1) & 1, status,
-                                       kDevTimeoutAccEmpty);
+            ok = ptx::mbar_wait_warp<kPair>(acc_empty_bar(buf), ((it - 2) >> 1) & 1, status,
+                                            kDevTimeoutAccEmpty);
         }
         if (!ok) break;
         tr.rec(kEvMmaAccGo, t, 0);
@@ -469,41 +486,47 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
         for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
           const int s = static_cast<int>(kit % kStages);
           tr.rec(kEvMmaFullWait, t, kb);
-          if (!ptx::mbar_wait(full_bar(s), (kit / kStages) & 1u, status, kDevTimeoutMma)) {
+          if (!ptx::mbar_wait_warp(full_bar(s), (kit / kStages) & 1u, status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
           tr.rec(kEvMmaFullGo, t, kb);
           ptx::tc_fence_after();
-          const uint32_t sa = smem + C::kOffA + s * C::kABytes;
-          const uint32_t sb = smem + C::kOffB + s * C::kBBytes;
-          const uint32_t ssfa = smem + C::kOffSFA + s * C::kSFABytes;
-          const uint32_t ssfb = smem + C::kOffSFB + s * C::kSFBBytes;
-          const uint32_t sf_off = static_cast<uint32_t>(kit % kSFBufs) * C::kSFBufCols;
-          const uint32_t sfa_t = tmem_base + C::kSFACol + sf_off;
-          const uint32_t sfb_t = tmem_base + C::kSFBCol + sf_off;
-          ptx::tmem_cp_32x128b_x4<kCtaGroup>(sfa_t, ptx::sf_chunk_desc(ssfa));
+          if (ptx::elect_one()) {
+            const uint32_t sa = smem + C::kOffA + s * C::kABytes;
+            const uint32_t sb = smem + C::kOffB + s * C::kBBytes;
+            const uint32_t ssfa = smem + C::kOffSFA + s * C::kSFABytes;
+            const uint32_t ssfb = smem + C::kOffSFB + s * C::kSFBBytes;
+            const uint32_t sf_off = static_cast<uint32_t>(kit % kSFBufs) * C::kSFBufCols;
+            const uint32_t sfa_t = tmem_base + C::kSFACol + sf_off;
+            const uint32_t sfb_t = tmem_base + C::kSFBCol + sf_off;
+            ptx::tmem_cp_32x128b_x4<kCtaGroup>(sfa_t, ptx::sf_chunk_desc(ssfa));
 #pragma unroll
-          for (int h = 0; h < kTileN / 128; ++h)
-            ptx::tmem_cp_32x128b_x4<kCtaGroup>(sfb_t + 4 * h, ptx::sf_chunk_desc(ssfb + 512 * h));
-          const uint64_t a_desc = ptx::kmajor_sw128_desc(sa);
-          const uint64_t b_desc = ptx::kmajor_sw128_desc(sb);
+            for (int h = 0; h < kTileN / 128; ++h)
+              ptx::tmem_cp_32x128b_x4<kCtaGroup>(sfb_t + 4 * h, ptx::sf_chunk_desc(ssfb + 512 * h));
+            const uint64_t a_desc = ptx::kmajor_sw128_desc(sa);
+            const uint64_t b_desc = ptx::kmajor_sw128_desc(sb);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            // Advance 32 bytes (one K=32 slice) inside the 128-byte swizzled rows.
-            ptx::mma_mxf8f6f4<kCtaGroup>(d_t, a_desc + 2 * j, b_desc + 2 * j,
-                                         ptx::with_scale_id(C::kIdesc, j),
-                                         sfa_t | (static_cast<uint32_t>(j) << 30),
-                                         sfb_t | (static_cast<uint32_t>(j) << 30),
-                                         (kb | j) != 0 ? 1u : 0u);
+            for (int j = 0; j < 4; ++j) {
+              // Advance 32 bytes (one K=32 slice) inside the 128-byte swizzled rows.
+              ptx::mma_mxf8f6f4<kCtaGroup>(d_t, a_desc + 2 * j, b_desc + 2 * j,
+                                           ptx::with_scale_id(C::kIdesc, j),
+                                           sfa_t | (static_cast<uint32_t>(j) << 30),
+                                           sfb_t | (static_cast<uint32_t>(j) << 30),
+                                           (kb | j) != 0 ? 1u : 0u);
+            }
+            ptx::tc_commit<kCtaGroup>(empty_bar(s));
+            if constexpr (kPair) ptx::tc_commit<kCtaGroup>(ptx::mapa(empty_bar(s), 1));
           }
-          ptx::tc_commit<kCtaGroup>(empty_bar(s));
-          if constexpr (kPair) ptx::tc_commit<kCtaGroup>(ptx::mapa(empty_bar(s), 1));
+          __syncwarp();
           tr.rec(kEvMmaIssued, t, kb);
         }
         if (!ok) break;
-        ptx::tc_commit<kCtaGroup>(acc_full_bar(buf));
-        if constexpr (kPair) ptx::tc_commit<kCtaGroup>(ptx::mapa(acc_full_bar(buf), 1));
+        if (ptx::elect_one()) {
+          ptx::tc_commit<kCtaGroup>(acc_full_bar(buf));
+          if constexpr (kPair) ptx::tc_commit<kCtaGroup>(ptx::mapa(acc_full_bar(buf), 1));
+        }
+        __syncwarp();
         tr.rec(kEvMmaTileDone, t, 0);
       }
       tr.rec(kEvEnd, 0, 0);

@@ -29,6 +29,12 @@ __device__ __forceinline__ uint32_t lane_id() {
   return r;
 }
 
+__device__ __forceinline__ uint64_t clock64() {
+  uint64_t c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -116,6 +122,23 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* st
       return false;
     }
   }
+}
+
+// True in exactly one lane of a converged warp (all 32 lanes must execute it).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// mbar_wait executed by every lane of a converged warp; the result is made
+// warp-uniform so the caller's control flow cannot diverge on a timeout.
+template <bool kClusterScope = false>
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int* status, int code) {
+  const bool ok = mbar_wait<kClusterScope>(bar, parity, status, code);
+  return __all_sync(0xffffffffu, ok) != 0;
 }
 
 // ---------------------------------------------------------------- TMA

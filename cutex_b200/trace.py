@@ -59,6 +59,16 @@ class GemmTrace:
     shape: tuple[int, int, int]
     config: dict[str, Any] = field(default_factory=dict)
     cta_times: list[tuple[int, int]] = field(default_factory=list)  # (start_ns, end_ns) per CTA
+    cta_cycles: list[tuple[int, int]] = field(default_factory=list)  # (start, end) SM cycle counter per CTA
+
+    def sm_clock_mhz(self) -> dict[str, float]:
+        """SM clock each CTA actually ran at: cycle-counter delta over timer delta."""
+
+        rates = sorted((ce - cs) / (te - ts) * 1e3 for (ts, te), (cs, ce) in zip(self.cta_times, self.cta_cycles)
+                       if ts and te > ts and ce > cs)
+        if not rates:
+            return {}
+        return {"ctas": len(rates), "min": rates[0], "median": rates[len(rates) // 2], "max": rates[-1]}
 
     def cta_spread(self) -> dict[str, float]:
         """How unevenly the persistent CTAs finish: end-time spread relative to the kernel span."""
@@ -96,7 +106,7 @@ class GemmTrace:
         """Per CTA and role: elapsed time and the total/mean of each wait span."""
 
         result: dict[str, Any] = {"shape": list(self.shape), "config": self.config, "ctas": {},
-                                  "cta_finish": self.cta_spread()}
+                                  "cta_finish": self.cta_spread(), "sm_clock_mhz": self.sm_clock_mhz()}
         for cta in sorted({e.cta for e in self.events}):
             per_role = {}
             for role in ROLES:
@@ -174,10 +184,10 @@ def run_gemm_trace(a, b, sfa, sfb, out, config=None, capacity: int = 1 << 16) ->
     from .kernels.dense_gemm import GemmConfig, _stream_handle, query
 
     cfg = config or GemmConfig(kernel=2, stages=6, epi_buffers=1, sf_buffers=1)
-    max_ctas = 1024
-    buf = torch.zeros(6 * (capacity + 1) * 2 + 2 * max_ctas, dtype=torch.int64, device=out.device)
     m, k = a.shape
     n = b.shape[0]
+    grid = query(m, n, k, cfg)["grid_ctas"]
+    buf = torch.zeros(6 * (capacity + 1) * 2 + 4 * grid, dtype=torch.int64, device=out.device)
     status = _lib.load().cutex_mxfp8_gemm_trace(
         a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), out.data_ptr(), m, n, k, out.stride(0),
         ctypes.byref(cfg.to_c()), buf.data_ptr(), capacity, _stream_handle(None))
@@ -188,9 +198,10 @@ def run_gemm_trace(a, b, sfa, sfb, out, config=None, capacity: int = 1 << 16) ->
     if not events:
         raise TraceError("the traced launch recorded no events")
     base = 6 * (capacity + 1) * 2
-    grid = query(m, n, k, cfg)["grid_ctas"]
-    cta_times = [(int(raw[base + 2 * c]), int(raw[base + 2 * c + 1])) for c in range(min(grid, max_ctas))]
-    return GemmTrace(events, capacity, (m, n, k), dict(cfg.__dict__), cta_times)
+    cta_times = [(int(raw[base + 2 * c]), int(raw[base + 2 * c + 1])) for c in range(grid)]
+    base += 2 * grid
+    cta_cycles = [(int(raw[base + 2 * c]), int(raw[base + 2 * c + 1])) for c in range(grid)]
+    return GemmTrace(events, capacity, (m, n, k), dict(cfg.__dict__), cta_times, cta_cycles)
 
 
 def disabled_trace_metadata() -> dict[str, Any]:

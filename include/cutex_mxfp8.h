@@ -130,11 +130,12 @@ CUTEX_API int cutex_mxfp8_query(const cutex_gemm_config* cfg, int64_t M, int64_t
 /*
  * Diagnostics: the same GEMM on an instrumented build of the kernel that
  * records per-role %globaltimer events of the first CTA (pair) into `trace`
- * (caller-allocated, 8-byte aligned, 6 * (trace_cap + 1) * 2 + 2 * grid_ctas
+ * (caller-allocated, 8-byte aligned, 6 * (trace_cap + 1) * 2 + 4 * grid_ctas
  * uint64 values, grid_ctas from cutex_mxfp8_query: regions [cta_rank * 3 +
  * role], role 0 = TMA producer, 1 = MMA issuer, 2 = epilogue warp 0; record 0
  * of a region = event count, record i = {time_ns, event << 56 | tile << 24 |
- * k_block}; then {start_ns, end_ns} of every CTA). Only configurations with an
+ * k_block}; then {start_ns, end_ns} of every CTA, then {start, end} of every
+ * CTA's SM cycle counter). Only configurations with an
  * instrumented twin are accepted (CUTEX_ERR_INVALID_ARGUMENT otherwise).
  * Replaces the reference's IKET in-kernel ranges (cutex/trace.py:96-175,
  * cutex/kernels/dense_gemm_v9.py:116-125); benchmark builds carry no tracing.

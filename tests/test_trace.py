@@ -45,6 +45,14 @@ def test_decode_and_summary_from_synthetic_records():
     assert disabled_trace_metadata()["benchmark_instrumented"] is False
 
 
+def test_sm_clock_from_cycle_counters():
+    tr = GemmTrace([], 1, (1, 1, 1), cta_times=[(1000, 2000), (1000, 3000), (0, 0)],
+                   cta_cycles=[(10, 1910), (5, 3805), (0, 0)])
+    clk = tr.sm_clock_mhz()
+    assert clk["ctas"] == 2 and clk["min"] == pytest.approx(1900.0) and clk["max"] == pytest.approx(1900.0)
+    assert GemmTrace([], 1, (1, 1, 1)).sm_clock_mhz() == {}
+
+
 def test_truncated_region_is_capped():
     cap = 2
     raw = _encode({(0, "mma"): [(1, 1, 0, 0), (2, 7, 0, 0)]}, cap)
@@ -76,3 +84,5 @@ def test_traced_launch_matches_and_records_every_stage():
         assert len(issued) == tiles * (K // 128) and tiles >= (2 if cfg.scheduler else 1)
         s = tr.summary()["ctas"][0]
         assert s["mma"]["elapsed_us"] > 0 and "wait loaded stage" in s["mma"]["spans"]
+        clk = tr.sm_clock_mhz()
+        assert clk["ctas"] >= 2 and 300.0 < clk["median"] < 2500.0
