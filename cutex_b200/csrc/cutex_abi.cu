@@ -166,12 +166,9 @@ Variant* find_variant(int cg, int bn, int stages, int epi, int sfb, int dynamic)
     if (stages != 0 && v.stages != stages) continue;
     if (epi != 0 && v.epi_bufs != epi) continue;
     if (sfb != 0 && v.sf_bufs != sfb) continue;
-    // Default (measured, burst, 2-CTA 256x256): 5 stages + 2 epilogue buffers + 1 SF
-    // buffer, then the deepest ring with one SF buffer.
-    auto rank = [](const Variant& x) {
-      const bool preferred = x.cta_group == 2 && x.tile_n == 256 && x.stages == 5 && x.epi_bufs == 2;
-      return (preferred && x.sf_bufs == 1 ? 10000 : 0) + x.stages * 100 + (x.sf_bufs == 1 ? 10 : 0) - x.epi_bufs;
-    };
+    // Default (measured, burst, 2-CTA 256x256 at 8192^3 and 16384^3): the deepest
+    // ring with one SF buffer and, at equal depth, the fewest epilogue buffers.
+    auto rank = [](const Variant& x) { return x.stages * 100 + (x.sf_bufs == 1 ? 10 : 0) - x.epi_bufs; };
     if (best == nullptr || rank(v) > rank(*best)) best = &v;
   }
   return best;
