@@ -82,6 +82,7 @@ enum TraceEvent : uint32_t {
   kEvEpiGo = 12,
   kEvEpiRelease = 13,
   kEvEpiTileDone = 14,
+  kEvEpiLoaded = 15,  // epilogue: first (overlapping) chunk read from TMEM
 };
 
 template <bool kOn>
@@ -101,6 +102,23 @@ struct Tracer {
     if constexpr (kOn) {
       if (region != nullptr && n < cap) {
         region[2 * (n + 1)] = ptx::globaltimer();
+        region[2 * (n + 1) + 1] = (static_cast<unsigned long long>(ev) << 56) |
+                                  (static_cast<unsigned long long>(tile & 0xFFFFFFF) << 24) |
+                                  static_cast<unsigned long long>(kb & 0xFFFFFF);
+        ++n;
+      }
+    }
+  }
+  // Timestamp now, record later (rec_at): keeps trace stores out of a stretch that
+  // ends in a release (a release would wait for the stores to become visible).
+  __device__ __forceinline__ unsigned long long stamp() const {
+    if constexpr (kOn) return region != nullptr ? ptx::globaltimer() : 0ull;
+    return 0ull;
+  }
+  __device__ __forceinline__ void rec_at(uint32_t ev, unsigned long long t_ns, int tile, int kb) {
+    if constexpr (kOn) {
+      if (region != nullptr && n < cap) {
+        region[2 * (n + 1)] = t_ns;
         region[2 * (n + 1) + 1] = (static_cast<unsigned long long>(ev) << 56) |
                                   (static_cast<unsigned long long>(tile & 0xFFFFFFF) << 24) |
                                   static_cast<unsigned long long>(kb & 0xFFFFFF);
@@ -549,7 +567,8 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
       const int buf = it & 1;
       tr.rec(kEvEpiWait, t, 0);
       if (!ptx::mbar_wait(acc_full_bar(buf), (it >> 1) & 1, status, kDevTimeoutEpilogue)) break;
-      tr.rec(kEvEpiGo, t, 0);
+      const unsigned long long t_go = tr.stamp();
+      unsigned long long t_loaded = 0;
       ptx::tc_fence_after();
       const uint32_t acc = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) +
                            static_cast<uint32_t>(buf ? C::kAcc1Col : 0);
@@ -562,14 +581,20 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
         ptx::tmem_ld_32x32b_x32(acc + c * 64 + 32, v1);
         ptx::tmem_wait_ld();
         const bool release = C::kOverlap ? (i == 0) : (i == C::kChunks - 1);
+        if (i == 0) t_loaded = tr.stamp();
         if (release) {
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) {
-            if constexpr (kPair) ptx::mbar_arrive_cluster(ptx::mapa(acc_empty_bar(buf), 0));
+            // The accumulator columns were read (wait::ld) and fenced; the
+            // barrier publishes no memory data, so a CTA-scope release suffices.
+            if constexpr (kPair) ptx::mbar_arrive_cluster_cta_release(ptx::mapa(acc_empty_bar(buf), 0));
             else ptx::mbar_arrive(acc_empty_bar(buf));
           }
-          tr.rec(kEvEpiRelease, t, 0);
+          const unsigned long long t_rel = tr.stamp();
+          tr.rec_at(kEvEpiGo, t_go, t, 0);
+          tr.rec_at(kEvEpiLoaded, t_loaded, t, 0);
+          tr.rec_at(kEvEpiRelease, t_rel, t, 0);
         }
         const uint32_t slot = chunk_ctr % kEpiBufs;
         if (chunk_ctr >= static_cast<uint32_t>(kEpiBufs)) {

@@ -85,6 +85,15 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
                : "memory");
 }
 
+// Arrive on a (possibly remote) cluster mbarrier with CTA-scope release. For
+// barriers that publish no generic-memory data, only completed work: e.g. TMEM
+// reads finished by tcgen05.wait::ld and ordered by
+// tcgen05.fence::before_thread_sync. A cluster-scope release there measured
+// ~1 us per arrive.
+__device__ __forceinline__ void mbar_arrive_cluster_cta_release(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
 template <bool kClusterScope>
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;

@@ -24,7 +24,7 @@ ROLES = ("producer", "mma", "epilogue")
 EVENTS = {
     1: "start", 2: "end", 3: "prod_wait", 4: "prod_go", 5: "mma_acc_wait", 6: "mma_acc_go",
     7: "mma_full_wait", 8: "mma_full_go", 9: "mma_issued", 10: "mma_tile_done",
-    11: "epi_wait", 12: "epi_go", 13: "epi_release", 14: "epi_tile_done",
+    11: "epi_wait", 12: "epi_go", 13: "epi_release", 14: "epi_tile_done", 15: "epi_loaded",
 }
 # (begin event, end event) -> span name
 SPANS = {
@@ -34,6 +34,7 @@ SPANS = {
     ("mma_full_go", "mma_issued"): "issue MMAs",
     ("epi_wait", "epi_go"): "wait accumulator full",
     ("epi_go", "epi_release"): "read overlap + release",
+    ("epi_go", "epi_loaded"): "read overlap chunk",
     ("epi_go", "epi_tile_done"): "drain tile",
 }
 
