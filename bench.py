@@ -9,9 +9,10 @@ D[:, r*N/g:(r+1)*N/g] from all of A and its slice of B), total work fixed.
 A step is one GEMM launch over resident inputs. Operands (256 MiB + 256 MiB
 E4M3 + scales at 1 GPU) exceed the 126 MB L2, so no L2 flush is done between
 steps. ``value`` = 2*M*N*K*steps / (max over ranks of the device time of the
-timed region). ``e2e`` repeats the measurement through the C ABI with pinned
-host buffers: each step copies A, B, SFA, SFB host->device, runs the GEMM and
-copies D device->host, all inside the CUDA-event timed interval.
+timed region). ``e2e`` repeats the measurement through the library's host-buffer
+entry (``cutex_mxfp8_gemm_host``) with pinned host buffers: each step copies A,
+B, SFA, SFB host->device, runs the GEMM in blocks and copies D device->host,
+copies and blocks overlapped, all inside the CUDA-event timed interval.
 
 ``--impl reference`` times the contract's CPU path (dequantise, fp32 matmul,
 cast to BF16: the oracle port) on the host cores, on bounded row/column
@@ -50,6 +51,8 @@ def parse_args():
     p.add_argument("--n", type=int, default=16384)
     p.add_argument("--k", type=int, default=16384)
     p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--e2e-blocks", type=int, default=4,
+                   help="host pipeline: output cut into up to BxB blocks (copies and GEMMs overlapped)")
     p.add_argument("--allgather", action="store_true", help="also time the NCCL all-gather of D (N > 1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--config", type=str, default="", help="native config as JSON, e.g. '{\"kernel\": 2}'")
@@ -435,29 +438,16 @@ def bench_cutex(args):
         hsa = sfa.cpu().pin_memory()
         hsb = sfb.cpu().pin_memory()
         hd = torch.empty(d.shape, dtype=d.dtype).pin_memory()
-        a2, b2, sa2, sb2 = torch.empty_like(a), torch.empty_like(b), torch.empty_like(sfa), torch.empty_like(sfb)
-        lib = _lib.load()
-        ccfg = cfg.to_c()
-        import ctypes
+        from cutex_b200.kernels import HostGemm
 
-        from cutex_b200.kernels.dense_gemm import workspace_for
-
-        ws_need = plan["workspace_bytes"]
-        ws = workspace_for(device, stream.cuda_stream, ws_need) if ws_need > 0 else None
-        ws_ptr, ws_len = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+        # The library's host-buffer entry: H2D copies, block GEMMs and D2H copies
+        # overlapped on its own streams, joined back into `stream`.
+        host_gemm = HostGemm(m, n_local, k, device=device, config=cfg, blocks=args.e2e_blocks)
 
         def e2e_step():
-            a2.copy_(ha, non_blocking=True)
-            b2.copy_(hb, non_blocking=True)
-            sa2.copy_(hsa, non_blocking=True)
-            sb2.copy_(hsb, non_blocking=True)
-            st = lib.cutex_mxfp8_gemm(a2.data_ptr(), b2.data_ptr(), sa2.data_ptr(), sb2.data_ptr(), d.data_ptr(),
-                                      m, n_local, k, n_local, ctypes.byref(ccfg), ws_ptr, ws_len,
-                                      stream.cuda_stream)
-            _lib.check(st, "cutex_mxfp8_gemm")
-            hd.copy_(d, non_blocking=True)
+            host_gemm(ha, hb, hsa, hsb, hd, stream=stream)
 
-        with torch.cuda.stream(stream):  # copies and the GEMM share one stream
+        with torch.cuda.stream(stream):
             e2e_step()
         torch.cuda.synchronize()
         if world > 1:
@@ -480,9 +470,10 @@ def bench_cutex(args):
             "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
             "steps": args.e2e_steps,
-            "path": "cutex_mxfp8_gemm C ABI, pinned host A/B/SFA/SFB in, D out",
+            "path": f"cutex_mxfp8_gemm_host C ABI (HostGemm, {args.e2e_blocks}x{args.e2e_blocks} blocks), "
+                    "pinned host A/B/SFA/SFB in, D out",
         }
-        del a2, b2, sa2, sb2, ha, hb, hsa, hsb, hd
+        del host_gemm, ha, hb, hsa, hsb, hd
 
     allgather = None
     if args.allgather and world > 1:

@@ -99,6 +99,10 @@ SIGNATURES = {
     ),
     "cutex_dense_gemm_v13": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _vp]),
     "cutex_mxfp8_gemm_skinny_static": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "cutex_mxfp8_gemm_host": (
+        ctypes.c_int,
+        [_vp] * 10 + [_i64, _i64, _i64, ctypes.POINTER(GemmConfigC), _i32, _vp, _i64, _vp],
+    ),
     "cutex_mxfp8_quantize": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
     "cutex_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "cutex_last_device_status": (ctypes.c_int, [_vp]),

@@ -702,3 +702,162 @@ extern "C" int cutex_mxfp8_gemm_skinny_static(const void* a, const void* b, cons
   return launch_skinny(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd, scratch,
                        reinterpret_cast<cudaStream_t>(stream));
 }
+
+// ---------------------------------------------------------------- host-buffer pipeline
+//
+// cutex_mxfp8_gemm_host: copies in, block GEMMs and copies out on three
+// library-owned streams per device, ordered by events. Streams and events are
+// created once per device (no device memory is allocated).
+
+namespace {
+
+constexpr int kMaxHostBlocks = 16;
+
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t h2d = nullptr, comp = nullptr, d2h = nullptr;
+  cudaEvent_t start = nullptr, end_h2d = nullptr, end_comp = nullptr, end_d2h = nullptr;
+  cudaEvent_t a_in[kMaxHostBlocks] = {}, b_in[kMaxHostBlocks] = {};
+  cudaEvent_t done[kMaxHostBlocks * kMaxHostBlocks] = {};
+};
+
+HostPipe g_pipes[kMaxDevices];
+std::mutex g_pipe_mutex;
+
+int host_pipe(int dev, HostPipe** out) {
+  HostPipe& p = g_pipes[dev];
+  if (!p.ready) {
+    const unsigned ev_flags = cudaEventDisableTiming;
+    bool ok = cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&p.comp, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&p.start, ev_flags) == cudaSuccess &&
+              cudaEventCreateWithFlags(&p.end_h2d, ev_flags) == cudaSuccess &&
+              cudaEventCreateWithFlags(&p.end_comp, ev_flags) == cudaSuccess &&
+              cudaEventCreateWithFlags(&p.end_d2h, ev_flags) == cudaSuccess;
+    for (int i = 0; ok && i < kMaxHostBlocks; ++i)
+      ok = cudaEventCreateWithFlags(&p.a_in[i], ev_flags) == cudaSuccess &&
+           cudaEventCreateWithFlags(&p.b_in[i], ev_flags) == cudaSuccess;
+    for (int i = 0; ok && i < kMaxHostBlocks * kMaxHostBlocks; ++i)
+      ok = cudaEventCreateWithFlags(&p.done[i], ev_flags) == cudaSuccess;
+    if (!ok) return CUTEX_ERR_CUDA;  // a later call retries the missing objects' creation
+    p.ready = true;
+  }
+  *out = &p;
+  return CUTEX_OK;
+}
+
+int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+extern "C" int cutex_mxfp8_gemm_host(const void* a_host, const void* b_host, const void* sfa_host,
+                                     const void* sfb_host, void* d_host, void* a_dev, void* b_dev,
+                                     void* sfa_dev, void* sfb_dev, void* d_dev, int64_t M, int64_t N,
+                                     int64_t K, const cutex_gemm_config* cfg, int32_t blocks,
+                                     void* workspace, int64_t workspace_bytes, cutex_stream_t stream) {
+  if (a_host == nullptr || b_host == nullptr || sfa_host == nullptr || sfb_host == nullptr ||
+      d_host == nullptr || a_dev == nullptr || b_dev == nullptr || sfa_dev == nullptr ||
+      sfb_dev == nullptr || d_dev == nullptr || workspace_bytes < 0)
+    return CUTEX_ERR_INVALID_ARGUMENT;
+  if (blocks < 1 || blocks > kMaxHostBlocks) return CUTEX_ERR_INVALID_ARGUMENT;
+  int st = validate_shape(M, N, K);
+  if (st != CUTEX_OK) return st;
+  if (!aligned16(a_dev) || !aligned16(b_dev) || !aligned16(sfa_dev) || !aligned16(sfb_dev) ||
+      !aligned16(d_dev))
+    return CUTEX_ERR_ALIGN;
+  DeviceState* ds = nullptr;
+  st = current_device_state(&ds);
+  if (st != CUTEX_OK) return st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
+  // Validate the configuration once on the whole shape.
+  Plan whole_plan{};
+  st = resolve_plan(cfg, M, N, K, ds->sm_count, &whole_plan);
+  if (st != CUTEX_OK) return st;
+
+  // Block sizes: multiples of 256 rows / columns (whole 128-row scale blocks,
+  // whole CTA-pair tiles); the last block of each dimension may be shorter.
+  const int64_t bm = std::max<int64_t>(256, ceil_div64(ceil_div64(M, blocks), 256) * 256);
+  const int64_t bn = std::max<int64_t>(256, ceil_div64(ceil_div64(N, blocks), 256) * 256);
+  const int gm = static_cast<int>(ceil_div64(M, bm));
+  const int gn = static_cast<int>(ceil_div64(N, bn));
+  const int64_t sf_row = K / 32;  // scale bytes per operand row
+  auto sf_bytes = [&](int64_t rows) { return ceil_div64(rows, 128) * 128 * sf_row; };
+  const char* ah = static_cast<const char*>(a_host);
+  const char* bh = static_cast<const char*>(b_host);
+  const char* sah = static_cast<const char*>(sfa_host);
+  const char* sbh = static_cast<const char*>(sfb_host);
+  char* dh = static_cast<char*>(d_host);
+  char* ad = static_cast<char*>(a_dev);
+  char* bd = static_cast<char*>(b_dev);
+  char* sad = static_cast<char*>(sfa_dev);
+  char* sbd = static_cast<char*>(sfb_dev);
+  char* dd = static_cast<char*>(d_dev);
+  const cudaStream_t user = reinterpret_cast<cudaStream_t>(stream);
+
+  std::lock_guard<std::mutex> lock(g_pipe_mutex);
+  HostPipe* p = nullptr;
+  st = host_pipe(dev, &p);
+  if (st != CUTEX_OK) return st;
+  bool ok = cudaEventRecord(p->start, user) == cudaSuccess &&
+            cudaStreamWaitEvent(p->h2d, p->start, 0) == cudaSuccess &&
+            cudaStreamWaitEvent(p->comp, p->start, 0) == cudaSuccess &&
+            cudaStreamWaitEvent(p->d2h, p->start, 0) == cudaSuccess;
+  int gemm_status = CUTEX_OK;
+  // One block GEMM and its D2H copy, after A panel i and B panel j have landed.
+  auto run_block = [&](int i, int j) {
+    const int64_t m0 = i * bm, n0 = j * bn;
+    const int64_t rows = std::min(bm, M - m0), cols = std::min(bn, N - n0);
+    const int64_t d_off = (m0 * N + n0) * 2;
+    ok = ok && cudaStreamWaitEvent(p->comp, p->a_in[i], 0) == cudaSuccess &&
+         cudaStreamWaitEvent(p->comp, p->b_in[j], 0) == cudaSuccess;
+    if (!ok || gemm_status != CUTEX_OK) return;
+    gemm_status = cutex_mxfp8_gemm(ad + m0 * K, bd + n0 * K, sad + m0 * sf_row, sbd + n0 * sf_row, dd + d_off,
+                                   rows, cols, K, N, cfg, workspace, workspace_bytes, p->comp);
+    cudaEvent_t e = p->done[i * gn + j];
+    ok = ok && cudaEventRecord(e, p->comp) == cudaSuccess &&
+         cudaStreamWaitEvent(p->d2h, e, 0) == cudaSuccess &&
+         cudaMemcpy2DAsync(dh + d_off, static_cast<size_t>(N) * 2, dd + d_off, static_cast<size_t>(N) * 2,
+                           static_cast<size_t>(cols) * 2, static_cast<size_t>(rows), cudaMemcpyDeviceToHost,
+                           p->d2h) == cudaSuccess;
+  };
+  // All copies in first (so the copy engine never waits for the host to
+  // enqueue block GEMMs), then the blocks in growing-square order.
+  const int steps = std::max(gm, gn);
+  for (int s = 0; ok && s < steps; ++s) {
+    if (s < gm) {
+      const int64_t m0 = s * bm, rows = std::min(bm, M - m0);
+      ok = cudaMemcpyAsync(ad + m0 * K, ah + m0 * K, static_cast<size_t>(rows * K), cudaMemcpyHostToDevice,
+                           p->h2d) == cudaSuccess &&
+           cudaMemcpyAsync(sad + m0 * sf_row, sah + m0 * sf_row, static_cast<size_t>(sf_bytes(rows)),
+                           cudaMemcpyHostToDevice, p->h2d) == cudaSuccess &&
+           cudaEventRecord(p->a_in[s], p->h2d) == cudaSuccess;
+    }
+    if (ok && s < gn) {
+      const int64_t n0 = s * bn, rows = std::min(bn, N - n0);
+      ok = cudaMemcpyAsync(bd + n0 * K, bh + n0 * K, static_cast<size_t>(rows * K), cudaMemcpyHostToDevice,
+                           p->h2d) == cudaSuccess &&
+           cudaMemcpyAsync(sbd + n0 * sf_row, sbh + n0 * sf_row, static_cast<size_t>(sf_bytes(rows)),
+                           cudaMemcpyHostToDevice, p->h2d) == cudaSuccess &&
+           cudaEventRecord(p->b_in[s], p->h2d) == cudaSuccess;
+    }
+  }
+  for (int s = 0; ok && gemm_status == CUTEX_OK && s < steps; ++s) {
+    // Every block whose larger index is s: row s against columns 0..s, then
+    // rows 0..s-1 against column s.
+    if (s < gm)
+      for (int j = 0; j <= std::min(s, gn - 1); ++j) run_block(s, j);
+    if (s < gn)
+      for (int i = 0; i < std::min(s, gm); ++i) run_block(i, s);
+  }
+  // Join: the caller's stream waits for all three streams, even after an error.
+  const bool joined = cudaEventRecord(p->end_h2d, p->h2d) == cudaSuccess &&
+                      cudaEventRecord(p->end_comp, p->comp) == cudaSuccess &&
+                      cudaEventRecord(p->end_d2h, p->d2h) == cudaSuccess &&
+                      cudaStreamWaitEvent(user, p->end_h2d, 0) == cudaSuccess &&
+                      cudaStreamWaitEvent(user, p->end_comp, 0) == cudaSuccess &&
+                      cudaStreamWaitEvent(user, p->end_d2h, 0) == cudaSuccess;
+  if (gemm_status != CUTEX_OK) return gemm_status;
+  return ok && joined ? CUTEX_OK : CUTEX_ERR_CUDA;
+}

@@ -8,6 +8,9 @@
   over native configurations, keyed by shape and device target) for
   ``cutex_b200.compile``.
 * ``query(m, n, k, config)``: what a launch would do (grid, SMEM, stages).
+* ``HostGemm(m, n, k)`` / ``dense_gemm_host``: the same GEMM from host buffers
+  to a host buffer, H2D copies, block GEMMs and D2H copies overlapped
+  (``cutex_mxfp8_gemm_host``).
 
 Operands: ``a`` [M, K] and ``b`` [N, K] E4M3 (``torch.float8_e4m3fn`` or
 ``uint8``), K-major and contiguous; ``sfa``/``sfb`` flat 128x4-swizzled E8M0
@@ -170,6 +173,71 @@ class PreparedGemm:
             _lib.check(status, "cutex_mxfp8_gemm")
 
 
+class HostGemm:
+    """GEMM from pinned host operands into a pinned host D through device staging buffers.
+
+    Holds device buffers for one shape (A, B, their scales, D) and calls
+    ``cutex_mxfp8_gemm_host``, which overlaps the host-to-device copies, the
+    block GEMMs and the device-to-host copy of each finished block. The call is
+    asynchronous on ``stream``: synchronise before reading ``d_host``.
+    """
+
+    def __init__(self, m: int, n: int, k: int, device=None, config: GemmConfig | None = None, blocks: int = 4):
+        import torch
+
+        validate_mxfp8_gemm_shape(m, n, k)
+        if not 1 <= blocks <= 16:
+            raise _lib.CutexArgumentError(_lib.CUTEX_ERR_INVALID_ARGUMENT, f"blocks must be in [1, 16], got {blocks}")
+        self.m, self.n, self.k, self.blocks = m, n, k, blocks
+        self.config = config or GemmConfig()
+        self._cfg = self.config.to_c()
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        u8 = torch.uint8
+        self.a = torch.empty(m, k, dtype=u8, device=dev)
+        self.b = torch.empty(n, k, dtype=u8, device=dev)
+        self.sfa = torch.empty(scale_buffer_bytes(m, k), dtype=u8, device=dev)
+        self.sfb = torch.empty(scale_buffer_bytes(n, k), dtype=u8, device=dev)
+        self.d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        self.device = dev
+        plan = query(m, n, k, self.config)
+        self.workspace = None
+        if plan["workspace_bytes"] > 0:
+            self.workspace = torch.empty(plan["workspace_bytes"], dtype=u8, device=dev)
+
+    @staticmethod
+    def _host(t, shape_bytes: int, name: str) -> int:
+        if t.device.type != "cpu" or not t.is_contiguous():
+            raise _lib.CutexArgumentError(_lib.CUTEX_ERR_INVALID_ARGUMENT, f"{name} must be a contiguous host tensor")
+        if t.numel() * t.element_size() < shape_bytes:
+            raise _lib.CutexArgumentError(_lib.CUTEX_ERR_INVALID_ARGUMENT, f"{name} holds fewer than {shape_bytes} bytes")
+        return t.data_ptr()
+
+    def __call__(self, a_host, b_host, sfa_host, sfb_host, d_host, stream=None) -> None:
+        m, n, k = self.m, self.n, self.k
+        ptrs = (
+            self._host(a_host, m * k, "a_host"),
+            self._host(b_host, n * k, "b_host"),
+            self._host(sfa_host, scale_buffer_bytes(m, k), "sfa_host"),
+            self._host(sfb_host, scale_buffer_bytes(n, k), "sfb_host"),
+            self._host(d_host, m * n * 2, "d_host"),
+        )
+        ws_ptr, ws_bytes = (None, 0) if self.workspace is None else (self.workspace.data_ptr(), self.workspace.numel())
+        status = _lib.load().cutex_mxfp8_gemm_host(
+            *ptrs, self.a.data_ptr(), self.b.data_ptr(), self.sfa.data_ptr(), self.sfb.data_ptr(),
+            self.d.data_ptr(), m, n, k, ctypes.byref(self._cfg), self.blocks, ws_ptr, ws_bytes,
+            _stream_handle(stream))
+        _lib.check(status, "cutex_mxfp8_gemm_host")
+
+
+def dense_gemm_host(a_host, b_host, sfa_host, sfb_host, d_host, stream=None, config: GemmConfig | None = None,
+                    blocks: int = 4) -> None:
+    """One-shot ``HostGemm`` (allocates the device staging buffers for this call)."""
+
+    m, k = a_host.shape
+    HostGemm(m, b_host.shape[0], k, config=config, blocks=blocks)(a_host, b_host, sfa_host, sfb_host, d_host,
+                                                                 stream=stream)
+
+
 def dense_gemm_v13(a_ptr: int, b_ptr: int, sfa_ptr: int, sfb_ptr: int, c_ptr: int,
                    max_active_clusters: int = 0, stream=None) -> None:
     """The reference's fixed M=N=K=16384 five-pointer launch, on the 2-CTA kernel."""
@@ -225,8 +293,10 @@ def mxfp8_gemm_launch(a, b, sfa, sfb, out, m, n, k, target, stream=None, *, kern
 __all__ = [
     "GEMM_CONFIGS",
     "GemmConfig",
+    "HostGemm",
     "PreparedGemm",
     "dense_gemm",
+    "dense_gemm_host",
     "dense_gemm_v13",
     "device_target",
     "mxfp8_gemm_launch",

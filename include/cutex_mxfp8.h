@@ -190,6 +190,33 @@ CUTEX_API int cutex_mxfp8_gemm_skinny_static(const void* a, const void* b, const
                                              const void* sfb, void* d, int64_t M, int64_t N,
                                              int64_t K, int64_t ldd, cutex_stream_t stream);
 
+/*
+ * The GEMM from host buffers to a host buffer: copies the operands to the
+ * caller's device buffers, runs the GEMM and copies D back, overlapped. The
+ * output is cut into up to blocks x blocks rectangles (rows and columns
+ * multiples of 256). The operand row panels are copied in a growing-square
+ * order (A panel s and B panel s, then every block whose larger index is s), so
+ * each block's GEMM starts as soon as its two panels have landed. Each finished
+ * block's D2H copy overlaps the remaining host-to-device copies.
+ *
+ * Host buffers: a_host [M, K] e4m3, b_host [N, K], sfa_host / sfb_host in the
+ * swizzled 128x4 layout (ceil(rows/128)*128*K/32 bytes), d_host [M, N] bf16
+ * (row pitch N). Use pinned (page-locked) host memory for the copies to
+ * overlap. Device buffers: the same sizes, 16-byte aligned, contents
+ * overwritten. `workspace` is passed to every block GEMM (only blocks with
+ * M <= 128 can use one). Ordering: starts after prior work on `stream`; work
+ * enqueued on `stream` afterwards runs after D has reached d_host. The copies
+ * and block GEMMs run on library-owned streams of the current device. Calls
+ * that share those streams are serialised.
+ * No reference counterpart: the reference always starts from device-resident
+ * TE tensors (cutex/kernels/modal_dense_gemm.py:375-406).
+ */
+CUTEX_API int cutex_mxfp8_gemm_host(const void* a_host, const void* b_host, const void* sfa_host,
+                                    const void* sfb_host, void* d_host, void* a_dev, void* b_dev,
+                                    void* sfa_dev, void* sfb_dev, void* d_dev, int64_t M, int64_t N,
+                                    int64_t K, const cutex_gemm_config* cfg, int32_t blocks,
+                                    void* workspace, int64_t workspace_bytes, cutex_stream_t stream);
+
 /* Human-readable text for a cutex_status value (static storage). */
 CUTEX_API const char* cutex_status_string(int status);
 

@@ -126,3 +126,14 @@ def test_python_wrapper_rejects_with_value_errors():
         query(200, 256, 256, GemmConfig(kernel=_lib.KERNEL_SKINNY))
     with pytest.raises(ValueError):
         query(16, 256, 256, GemmConfig(kernel=_lib.KERNEL_SKINNY, split_k=2))
+
+
+def test_host_gemm_argument_checks_without_a_device():
+    from cutex_b200.kernels import HostGemm
+
+    with pytest.raises(_lib.CutexArgumentError):
+        HostGemm(256, 256, 128, blocks=0)
+    with pytest.raises(_lib.CutexArgumentError):
+        HostGemm(256, 256, 128, blocks=17)
+    with pytest.raises(ValueError):
+        HostGemm(256, 250, 128)  # N not a multiple of 16
