@@ -211,6 +211,7 @@ struct Plan {
   int grid_ctas;
   int num_m_tiles, num_n_tiles, num_tiles;
   int streamk;                // skinny: stream-K split over the grid (needs workspace)
+  int dp_tiles;               // skinny stream-K: tiles taken whole before the split range
   int64_t workspace_bytes;    // skinny stream-K: partial slots + tile counters
   int64_t ws_partials_bytes;  // offset of the counters inside the workspace
 };
@@ -259,13 +260,16 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   plan->skinny = nullptr;
   plan->variant = nullptr;
   plan->streamk = 0;
+  plan->dp_tiles = 0;
   plan->workspace_bytes = 0;
   plan->ws_partials_bytes = 0;
   if (kernel == CUTEX_KERNEL_SKINNY) {
     SkinnyVariant* sv = find_skinny(M);
     if (sv == nullptr) return CUTEX_ERR_SHAPE;  // the skinny kernel covers M <= 128
     if (cfg.stages != 0 && cfg.stages != sv->stages) return CUTEX_ERR_INVALID_ARGUMENT;
-    if (cfg.split_k > 1) return CUTEX_ERR_INVALID_ARGUMENT;  // 0 = stream-K, 1 = no split
+    // 0 = stream-K (library choice of full data-parallel waves), 1 = no split,
+    // 2 = pure stream-K, 3 = full data-parallel waves + stream-K remainder.
+    if (cfg.split_k > 3) return CUTEX_ERR_INVALID_ARGUMENT;
     plan->skinny = sv;
     plan->kernel = kernel;
     plan->tile_n = 128;
@@ -284,6 +288,8 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
     plan->streamk = (cfg.split_k == 1 || auto_whole) ? 0 : 1;
     grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, plan->streamk ? units : plan->num_n_tiles)));
     plan->grid_ctas = grid;
+    plan->dp_tiles = 0;
+    if (plan->streamk && cfg.split_k == 3) plan->dp_tiles = plan->num_n_tiles / grid * grid;
     if (plan->streamk)
       skinny_workspace(sm_count, plan->num_n_tiles, &plan->ws_partials_bytes, &plan->workspace_bytes);
     return CUTEX_OK;
@@ -415,7 +421,8 @@ int launch_skinny(const Plan& plan, int dev, const void* a, const void* b, const
   args.N = static_cast<int>(N);
   args.num_n_tiles = plan.num_n_tiles;
   args.num_k_blocks = static_cast<int>(K / 128);
-  args.units = static_cast<long long>(plan.num_n_tiles) * args.num_k_blocks;
+  args.dp_tiles = plan.streamk ? plan.dp_tiles : 0;
+  args.units = static_cast<long long>(plan.num_n_tiles - args.dp_tiles) * args.num_k_blocks;
   args.streamk = plan.streamk;
   args.ldd = ldd;
   args.d = static_cast<__nv_bfloat16*>(d);

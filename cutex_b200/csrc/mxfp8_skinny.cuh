@@ -5,15 +5,16 @@
 //   padded M (kNPad = 16..128). B is read once from HBM (evict-first), A and its
 //   scales stay L2-resident (evict-last) and are re-read per K-stage.
 //
-// Work split (stream-K): the (N-tile, K-stage) units are cut into gridDim.x
-// equal contiguous ranges, one per CTA, so every SM streams the same number of
-// bytes. A CTA that covers a whole tile writes BF16 D directly. A tile cut
-// between CTAs is finished through a workspace: each contributor stores its
-// FP32 partial in its own slot, then increments the tile's arrival counter; the
-// contributor that arrives last sums all partials in contributor order
-// (deterministic), writes D, and resets the counter to zero for the next call.
-// Nobody waits for another CTA. Without a workspace (split disabled) CTAs take
-// whole tiles round-robin.
+// Work split: the first dp_tiles tiles go whole, round-robin over the grid
+// (data-parallel waves); the (N-tile, K-stage) units of the remaining tiles are
+// cut into gridDim.x equal contiguous ranges, one per CTA (stream-K), so every
+// SM streams the same number of bytes. dp_tiles = 0 is pure stream-K,
+// dp_tiles = all tiles is pure data-parallel. A CTA that covers a whole tile
+// writes BF16 D directly. A tile cut between CTAs is finished through a
+// workspace: each contributor stores its FP32 partial in its own slot, then
+// increments the tile's arrival counter; the contributor that arrives last sums
+// all partials in contributor order (deterministic), writes D, and resets the
+// counter to zero for the next call. Nobody waits for another CTA.
 //
 // Warp roles (192 threads) as in the large kernel: warps 0-3 epilogue (TMEM lane
 // quarter w = rows 32w..32w+31 of the B tile), warp 4 MMA issuer, warp 5 TMA.
@@ -33,8 +34,9 @@ struct SkinnyArgs {
   int N;              // rows of B
   int num_n_tiles;    // ceil(N / 128)
   int num_k_blocks;   // K / 128
-  long long units;    // num_n_tiles * num_k_blocks
-  int streamk;        // 1: stream-K split over gridDim.x CTAs; 0: whole tiles round-robin
+  long long units;    // stream-K units: (num_n_tiles - dp_tiles) * num_k_blocks
+  int streamk;        // 1: stream-K over the tiles from dp_tiles on; 0: whole tiles round-robin
+  int dp_tiles;       // tiles [0, dp_tiles) whole, round-robin (stream-K mode)
   long long ldd;      // row stride of D (elements)
   __nv_bfloat16* d;
   float* partials;    // [2 * gridDim.x][kNPad][128] fp32 slots (stream-K only)
@@ -73,35 +75,39 @@ __device__ __forceinline__ long long sk_owner(long long u, long long P, long lon
   return ((u + 1) * P - 1) / U;
 }
 
-// Walks a CTA's segments: (tile, first K-stage, end K-stage) in order.
+// Walks a CTA's segments: (tile, first K-stage, end K-stage) in order; whole
+// round-robin tiles first, then the CTA's stream-K range.
 struct SegmentWalker {
-  long long u, u_end;
-  int tile_rr;  // round-robin tile for the non-split mode
+  long long u, u_end;  // stream-K units (relative to tile dp_tiles)
+  int tile_rr;         // next round-robin tile
+  int rr_end;          // round-robin tiles end here
   __device__ __forceinline__ void init(const SkinnyArgs& a) {
+    tile_rr = blockIdx.x;
     if (a.streamk) {
+      rr_end = a.dp_tiles;
       u = sk_start(blockIdx.x, gridDim.x, a.units);
       u_end = sk_start(blockIdx.x + 1, gridDim.x, a.units);
     } else {
-      tile_rr = blockIdx.x;
+      rr_end = a.num_n_tiles;
       u = 0;
       u_end = 0;
     }
   }
   __device__ __forceinline__ bool next(const SkinnyArgs& a, int& tile, int& kb0, int& kb1) {
-    if (a.streamk) {
-      if (u >= u_end) return false;
-      tile = static_cast<int>(u / a.num_k_blocks);
-      kb0 = static_cast<int>(u - static_cast<long long>(tile) * a.num_k_blocks);
-      const long long left = u_end - u;
-      kb1 = static_cast<int>(min(static_cast<long long>(a.num_k_blocks), kb0 + left));
-      u += kb1 - kb0;
+    if (tile_rr < rr_end) {
+      tile = tile_rr;
+      tile_rr += gridDim.x;
+      kb0 = 0;
+      kb1 = a.num_k_blocks;
       return true;
     }
-    if (tile_rr >= a.num_n_tiles) return false;
-    tile = tile_rr;
-    tile_rr += gridDim.x;
-    kb0 = 0;
-    kb1 = a.num_k_blocks;
+    if (u >= u_end) return false;
+    const int rel = static_cast<int>(u / a.num_k_blocks);
+    tile = a.dp_tiles + rel;
+    kb0 = static_cast<int>(u - static_cast<long long>(rel) * a.num_k_blocks);
+    const long long left = u_end - u;
+    kb1 = static_cast<int>(min(static_cast<long long>(a.num_k_blocks), kb0 + left));
+    u += kb1 - kb0;
     return true;
   }
 };
@@ -231,7 +237,7 @@ __global__ void __launch_bounds__(192, 1)
     const int P = gridDim.x;
     const long long U = args.units;
     const int first_tile =
-        args.streamk ? static_cast<int>(sk_start(blockIdx.x, P, U) / args.num_k_blocks) : -1;
+        args.streamk ? args.dp_tiles + static_cast<int>(sk_start(blockIdx.x, P, U) / args.num_k_blocks) : -1;
     const uint32_t tid = threadIdx.x;  // 0..127: row of the B tile = column of D
     int seg = 0;
     while (walk.next(args, tile, kb0, kb1)) {
@@ -261,8 +267,13 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
         } else {
+          // Slot layout [kNPad / 4][128 rows][4 columns]: one 16-byte store per
+          // thread and column group, 512 contiguous bytes per warp.
+          float4* part4 = reinterpret_cast<float4*>(part);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) part[(c + j) * 128 + tid] = __uint_as_float(v[j]);
+          for (int q = 0; q < 4; ++q)
+            part4[(c / 4 + q) * 128 + tid] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                                         __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
         }
       }
       ptx::tc_fence_before();
@@ -272,7 +283,7 @@ __global__ void __launch_bounds__(192, 1)
         // Publish the partial, count arrivals; the last contributor reduces.
         __threadfence();
         ptx::named_barrier(1, 128);
-        const long long t_u0 = static_cast<long long>(tile) * args.num_k_blocks;
+        const long long t_u0 = static_cast<long long>(tile - args.dp_tiles) * args.num_k_blocks;
         const int c0 = static_cast<int>(sk_owner(t_u0, P, U));
         const int c1 = static_cast<int>(sk_owner(t_u0 + args.num_k_blocks - 1, P, U));
         if (tid == 0) {
@@ -282,23 +293,53 @@ __global__ void __launch_bounds__(192, 1)
         ptx::named_barrier(1, 128);
         if (slot[1] != 0u) {
           __threadfence();
+          // Sum the contributors' slots in contributor order (deterministic). The
+          // loop is latency-bound, so each pass covers up to 64 columns and keeps
+          // two contributors' loads (2 x 16 float4 per thread) in flight.
+          auto slot_of = [&](int cc) {
+            const int ft = args.dp_tiles + static_cast<int>(sk_start(cc, P, U) / args.num_k_blocks);
+            const int s = (ft == tile) ? 2 * cc : 2 * cc + 1;
+            return reinterpret_cast<const float4*>(args.partials + static_cast<size_t>(s) * kNPad * 128);
+          };
+          constexpr int kPass = kNPad < 64 ? kNPad : 64;  // columns per pass
+          constexpr int kQ = kPass / 4;                    // float4 per thread per pass
+          const int nc = c1 - c0 + 1;
 #pragma unroll 1
-          for (int c = 0; c < kNPad; c += 16) {
-            float sum[16];
+          for (int c = 0; c < kNPad; c += kPass) {
+            float4 sum[kQ];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) sum[j] = 0.f;
-            for (int cc = c0; cc <= c1; ++cc) {
-              const int ft = static_cast<int>(sk_start(cc, P, U) / args.num_k_blocks);
-              const int s = (ft == tile) ? 2 * cc : 2 * cc + 1;
-              const float* src = args.partials + static_cast<size_t>(s) * kNPad * 128;
+            for (int q = 0; q < kQ; ++q) sum[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            int i = 0;
+            for (; i + 1 < nc; i += 2) {
+              const float4* sx = slot_of(c0 + i);
+              const float4* sy = slot_of(c0 + i + 1);
+              float4 x[kQ], y[kQ];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) sum[j] += __ldcg(src + (c + j) * 128 + tid);
+              for (int q = 0; q < kQ; ++q) x[q] = __ldcg(sx + (c / 4 + q) * 128 + tid);
+#pragma unroll
+              for (int q = 0; q < kQ; ++q) y[q] = __ldcg(sy + (c / 4 + q) * 128 + tid);
+#pragma unroll
+              for (int q = 0; q < kQ; ++q) {
+                sum[q].x += x[q].x; sum[q].y += x[q].y; sum[q].z += x[q].z; sum[q].w += x[q].w;
+                sum[q].x += y[q].x; sum[q].y += y[q].y; sum[q].z += y[q].z; sum[q].w += y[q].w;
+              }
+            }
+            if (i < nc) {
+              const float4* sx = slot_of(c0 + i);
+              float4 x[kQ];
+#pragma unroll
+              for (int q = 0; q < kQ; ++q) x[q] = __ldcg(sx + (c / 4 + q) * 128 + tid);
+#pragma unroll
+              for (int q = 0; q < kQ; ++q) {
+                sum[q].x += x[q].x; sum[q].y += x[q].y; sum[q].z += x[q].z; sum[q].w += x[q].w;
+              }
             }
             if (n < args.N) {
+              const float* f = reinterpret_cast<const float*>(sum);
 #pragma unroll
-              for (int j = 0; j < 16; ++j)
+              for (int j = 0; j < kPass; ++j)
                 if (c + j < args.M)
-                  args.d[static_cast<long long>(c + j) * args.ldd + n] = __float2bfloat16_rn(sum[j]);
+                  args.d[static_cast<long long>(c + j) * args.ldd + n] = __float2bfloat16_rn(f[j]);
             }
           }
           if (tid == 0) args.counters[tile] = 0u;

@@ -125,7 +125,7 @@ def test_python_wrapper_rejects_with_value_errors():
     with pytest.raises(ValueError):
         query(200, 256, 256, GemmConfig(kernel=_lib.KERNEL_SKINNY))
     with pytest.raises(ValueError):
-        query(16, 256, 256, GemmConfig(kernel=_lib.KERNEL_SKINNY, split_k=2))
+        query(16, 256, 256, GemmConfig(kernel=_lib.KERNEL_SKINNY, split_k=4))
 
 
 def test_host_gemm_argument_checks_without_a_device():
