@@ -174,30 +174,32 @@ Variant* find_variant(int cg, int bn, int stages, int epi, int sfb, int dynamic)
   return best;
 }
 
-// Skinny (M <= 128) kernels: (padded M, stages).
+// Skinny (M <= 128) kernels: (padded M, stages, 128-row B tiles per CTA tile).
 struct SkinnyVariant {
-  int npad, stages, smem_bytes;
+  int npad, stages, tiles, smem_bytes;
   const void* fn;
   bool attr_set[kMaxDevices];
 };
 
-template <int NP, int S>
+template <int NP, int S, int T = 1>
 SkinnyVariant make_skinny() {
   SkinnyVariant v{};
   v.npad = NP;
   v.stages = S;
-  v.smem_bytes = SkinnyCfg<NP, S>::kSmemBytes;
-  v.fn = reinterpret_cast<const void*>(&mxfp8_skinny_kernel<NP, S>);
+  v.tiles = T;
+  v.smem_bytes = SkinnyCfg<NP, S, T>::kSmemBytes;
+  v.fn = reinterpret_cast<const void*>(&mxfp8_skinny_kernel<NP, S, T>);
   return v;
 }
 
 SkinnyVariant g_skinny[] = {
-    make_skinny<16, 10>(), make_skinny<32, 10>(), make_skinny<64, 8>(), make_skinny<128, 6>(),
+    make_skinny<16, 10>(),    make_skinny<32, 10>(),    make_skinny<64, 8>(), make_skinny<128, 6>(),
+    make_skinny<64, 5, 2>(), make_skinny<128, 4, 2>(),
 };
 
-SkinnyVariant* find_skinny(int64_t M) {
+SkinnyVariant* find_skinny(int64_t M, int tiles) {
   for (auto& v : g_skinny)
-    if (M <= v.npad) return &v;
+    if (M <= v.npad && v.tiles == tiles) return &v;
   return nullptr;
 }
 
@@ -264,28 +266,38 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   plan->workspace_bytes = 0;
   plan->ws_partials_bytes = 0;
   if (kernel == CUTEX_KERNEL_SKINNY) {
-    SkinnyVariant* sv = find_skinny(M);
-    if (sv == nullptr) return CUTEX_ERR_SHAPE;  // the skinny kernel covers M <= 128
-    if (cfg.stages != 0 && cfg.stages != sv->stages) return CUTEX_ERR_INVALID_ARGUMENT;
     // 0 = stream-K (library choice of full data-parallel waves), 1 = no split,
     // 2 = pure stream-K, 3 = full data-parallel waves + stream-K remainder.
     if (cfg.split_k > 3) return CUTEX_ERR_INVALID_ARGUMENT;
+    if (cfg.tile_n != 0 && cfg.tile_n != 128 && cfg.tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
+    SkinnyVariant* sv1 = find_skinny(M, 1);
+    if (sv1 == nullptr) return CUTEX_ERR_SHAPE;  // the skinny kernel covers M <= 128
+    int grid = sm_count;
+    if (cfg.max_ctas != 0) grid = std::min(grid, cfg.max_ctas);
+    const int64_t tiles128 = (N + 127) / 128;
+    // Split-K pays off while the fp32 partial slots stay small (padded M <= 32);
+    // for wider M the AUTO choice keeps whole tiles (measured: M = 128, N = 28672,
+    // K = 8192 streams at 0.77 of HBM with whole 128-row tiles vs 0.64 split).
+    const bool auto_whole = cfg.kernel == CUTEX_KERNEL_AUTO && cfg.split_k == 0 && sv1->npad > 32;
+    // Two 128-row B tiles per CTA tile (tile_n 256, whole tiles only): one A
+    // stage serves both tiles. Explicit only: measured at M = 64 / 128,
+    // N = 28672, K = 8192 it streams 3-5 % slower than single tiles (one wave of
+    // 112 CTAs at the same per-SM rate instead of 148 + 76).
+    const int tiles = cfg.tile_n == 256 ? 2 : 1;
+    SkinnyVariant* sv = find_skinny(M, tiles);
+    if (sv == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;  // no double-tile build for this padded M
+    if (tiles == 2 && cfg.split_k > 1) return CUTEX_ERR_INVALID_ARGUMENT;
+    if (cfg.stages != 0 && cfg.stages != sv->stages) return CUTEX_ERR_INVALID_ARGUMENT;
     plan->skinny = sv;
     plan->kernel = kernel;
-    plan->tile_n = 128;
+    plan->tile_n = 128 * tiles;
     plan->num_m_tiles = 1;
-    plan->num_n_tiles = static_cast<int>((N + 127) / 128);
+    plan->num_n_tiles = static_cast<int>((tiles128 + tiles - 1) / tiles);
     plan->num_tiles = plan->num_n_tiles;
     plan->raster_group = 1;
     plan->raster_along_n = 0;
     const int64_t units = static_cast<int64_t>(plan->num_n_tiles) * (K / 128);
-    int grid = sm_count;
-    if (cfg.max_ctas != 0) grid = std::min(grid, cfg.max_ctas);
-    // Split-K pays off while the fp32 partial slots stay small (padded M <= 32);
-    // for wider M the AUTO choice keeps whole tiles (measured: M = 128, N = 28672,
-    // K = 8192 streams at 0.77 of HBM with whole tiles vs 0.64 split).
-    const bool auto_whole = cfg.kernel == CUTEX_KERNEL_AUTO && cfg.split_k == 0 && sv->npad > 32;
-    plan->streamk = (cfg.split_k == 1 || auto_whole) ? 0 : 1;
+    plan->streamk = (cfg.split_k == 1 || auto_whole || tiles == 2) ? 0 : 1;
     grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, plan->streamk ? units : plan->num_n_tiles)));
     plan->grid_ctas = grid;
     plan->dp_tiles = 0;
@@ -404,8 +416,9 @@ int launch_skinny(const Plan& plan, int dev, const void* a, const void* b, const
                   void* workspace, cudaStream_t stream) {
   SkinnyVariant* v = plan.skinny;
   CUtensorMap tb, ta, tsb, tsa;
-  if (!encode_operand(&tb, b, N, K, 128) || !encode_operand(&ta, a, M, K, static_cast<uint32_t>(v->npad)) ||
-      !encode_scales(&tsb, sfb, N, K, 1) || !encode_scales(&tsa, sfa, M, K, 1))
+  if (!encode_operand(&tb, b, N, K, static_cast<uint32_t>(128 * v->tiles)) ||
+      !encode_operand(&ta, a, M, K, static_cast<uint32_t>(v->npad)) ||
+      !encode_scales(&tsb, sfb, N, K, static_cast<uint32_t>(v->tiles)) || !encode_scales(&tsa, sfa, M, K, 1))
     return CUTEX_ERR_CUDA;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
@@ -464,7 +477,7 @@ extern "C" int cutex_mxfp8_query(const cutex_gemm_config* cfg, int64_t M, int64_
   info->raster_group = plan.raster_group;
   if (plan.skinny != nullptr) {
     info->tile_m = plan.skinny->npad;  // padded M: the MMA's N side
-    info->tile_n = 128;
+    info->tile_n = plan.tile_n;
     info->stages = plan.skinny->stages;
     info->cluster_size = 1;
     info->smem_bytes = plan.skinny->smem_bytes;

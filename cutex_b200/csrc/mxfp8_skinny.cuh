@@ -16,10 +16,15 @@
 // all partials in contributor order (deterministic), writes D, and resets the
 // counter to zero for the next call. Nobody waits for another CTA.
 //
+// A CTA tile is kTiles x 128 rows of B (kTiles = 2: two MMAs per K-step share
+// the A stage, which halves A's L2 traffic and leaves more of the stage ring to
+// B; whole tiles only, since the split path's slots hold one 128-row tile).
+//
 // Warp roles (192 threads) as in the large kernel: warps 0-3 epilogue (TMEM lane
-// quarter w = rows 32w..32w+31 of the B tile), warp 4 MMA issuer, warp 5 TMA.
-// TMEM: two kNPad-column accumulators (per segment, alternating) + scale
-// columns (MMA-A scales = B's chunk, MMA-B scales = A's chunk) in two buffers.
+// quarter w = rows 32w..32w+31 of each 128-row B tile), warp 4 MMA issuer,
+// warp 5 TMA. TMEM: one or two accumulators of kTiles x kNPad columns (two when
+// they fit beside the scales, alternating by segment) + scale columns (MMA-A
+// scales = B's chunks, MMA-B scales = A's chunk) in two buffers.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -43,25 +48,32 @@ struct SkinnyArgs {
   unsigned int* counters;  // [num_n_tiles] arrival counters, zero between calls
 };
 
-template <int kNPad, int kStages>
+template <int kNPad, int kStages, int kTiles = 1>
 struct SkinnyCfg {
-  static constexpr int kBBytes = 128 * 128;        // one 128-row x 128-K tile of B
-  static constexpr int kABytes = kNPad * 128;      // kNPad rows of A
-  static constexpr int kStageBytes = kBBytes + kABytes + 512 + 512;
+  static constexpr int kBBytes = kTiles * 128 * 128;  // kTiles 128-row x 128-K tiles of B
+  static constexpr int kABytes = kNPad * 128;          // kNPad rows of A
+  static constexpr int kSFBBytes = kTiles * 512;
+  static constexpr int kStageBytes = kBBytes + kABytes + kSFBBytes + 512;
   static constexpr int kOffB = 0;
   static constexpr int kOffA = kOffB + kStages * kBBytes;
-  static constexpr int kOffSFB = kOffA + kStages * kABytes;  // B's scale chunk (MMA A side)
-  static constexpr int kOffSFA = kOffSFB + kStages * 512;    // A's scale chunk (MMA B side)
+  static constexpr int kOffSFB = kOffA + kStages * kABytes;  // B's scale chunks (MMA A side)
+  static constexpr int kOffSFA = kOffSFB + kStages * kSFBBytes;  // A's scale chunk (MMA B side)
   static constexpr int kOffBar = align_up(kOffSFA + kStages * 512, 8);
   static constexpr int kNumBars = 2 * kStages + 4;
   static constexpr int kOffSlot = kOffBar + kNumBars * 8;  // TMEM address + last-arrival flag
   static constexpr int kSmemBytes = kOffSlot + 16 + 1024;
   static constexpr int kTmemCols = 512;
-  static constexpr int kAcc1Col = 128;
-  static constexpr int kSFCol = 256;  // two buffers of 8 columns: [B chunk 4 | A chunk 4]
+  static constexpr int kAccCols = kTiles * kNPad;
+  static constexpr int kSFBufCols = 16;  // [B chunks 4 * kTiles | A chunk 4]
+  static constexpr int kAccBufs = 2 * kAccCols + 2 * kSFBufCols <= kTmemCols ? 2 : 1;
+  static constexpr int kAcc1Col = kAccCols;
+  static constexpr int kSFCol = kAccBufs * kAccCols;  // two buffers of kSFBufCols columns
   static constexpr uint32_t kTxBytes = kStageBytes;
   static constexpr uint32_t kIdesc = ptx::mxf8_idesc(128, kNPad);
   static_assert(kNPad % 16 == 0 && kNPad >= 16 && kNPad <= 128, "padded M");
+  static_assert(kTiles == 1 || kTiles == 2, "B tiles per CTA tile");
+  static_assert(4 * kTiles + 4 <= kSFBufCols, "scale columns");
+  static_assert(kSFCol + 2 * kSFBufCols <= kTmemCols, "TMEM plan");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
 };
 
@@ -112,13 +124,13 @@ struct SegmentWalker {
   }
 };
 
-template <int kNPad, int kStages>
+template <int kNPad, int kStages, int kTiles = 1>
 __global__ void __launch_bounds__(192, 1)
     mxfp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_a,
                         const __grid_constant__ CUtensorMap tmap_sfb,
                         const __grid_constant__ CUtensorMap tmap_sfa, const SkinnyArgs args) {
-  using C = SkinnyCfg<kNPad, kStages>;
+  using C = SkinnyCfg<kNPad, kStages, kTiles>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = ptx::smem_u32(smem_raw);
   const uint32_t smem = (raw_base + 1023u) & ~1023u;
@@ -178,9 +190,10 @@ __global__ void __launch_bounds__(192, 1)
           }
           const uint32_t fb = full_bar(s);
           ptx::mbar_arrive_expect_tx(fb, C::kTxBytes);
-          ptx::tma_load_2d(smem + C::kOffB + s * C::kBBytes, &tmap_b, fb, kb * 128, tile * 128, stream_pol);
+          ptx::tma_load_2d(smem + C::kOffB + s * C::kBBytes, &tmap_b, fb, kb * 128, tile * 128 * kTiles,
+                           stream_pol);
           ptx::tma_load_2d(smem + C::kOffA + s * C::kABytes, &tmap_a, fb, kb * 128, 0, keep_pol);
-          ptx::tma_load_3d(smem + C::kOffSFB + s * 512, &tmap_sfb, fb, 0, kb, tile, stream_pol);
+          ptx::tma_load_3d(smem + C::kOffSFB + s * C::kSFBBytes, &tmap_sfb, fb, 0, kb, tile * kTiles, stream_pol);
           ptx::tma_load_3d(smem + C::kOffSFA + s * 512, &tmap_sfa, fb, 0, kb, 0, keep_pol);
         }
       }
@@ -199,9 +212,10 @@ __global__ void __launch_bounds__(192, 1)
       int seg = 0;
       bool ok = true;
       while (ok && walk.next(args, tile, kb0, kb1)) {
-        const int buf = seg & 1;
-        if (seg >= 2 &&
-            !ptx::mbar_wait(acc_empty_bar(buf), ((seg - 2) >> 1) & 1, status, kDevTimeoutAccEmpty))
+        // Accumulator buffer `buf` is used for the use-th time by this segment.
+        const int buf = seg % C::kAccBufs, use = seg / C::kAccBufs;
+        if (use >= 1 &&
+            !ptx::mbar_wait(acc_empty_bar(buf), (use - 1) & 1, status, kDevTimeoutAccEmpty))
           break;
         ptx::tc_fence_after();
         const uint32_t d_t = tmem_base + (buf ? C::kAcc1Col : 0);
@@ -212,17 +226,23 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t sf_t = tmem_base + C::kSFCol + (kit & 1u) * 8u;
-          ptx::tmem_cp_32x128b_x4<1>(sf_t, ptx::sf_chunk_desc(smem + C::kOffSFB + s * 512));
-          ptx::tmem_cp_32x128b_x4<1>(sf_t + 4, ptx::sf_chunk_desc(smem + C::kOffSFA + s * 512));
-          const uint64_t a_desc = ptx::kmajor_sw128_desc(smem + C::kOffB + s * C::kBBytes);
+          // Scale buffer: [B tile chunks 4 * kTiles columns | A chunk 4 columns].
+          const uint32_t sf_t = tmem_base + C::kSFCol + (kit & 1u) * C::kSFBufCols;
+          const uint32_t sfa_t = sf_t + 4 * kTiles;
+#pragma unroll
+          for (int t = 0; t < kTiles; ++t)
+            ptx::tmem_cp_32x128b_x4<1>(sf_t + 4 * t, ptx::sf_chunk_desc(smem + C::kOffSFB + s * C::kSFBBytes + 512 * t));
+          ptx::tmem_cp_32x128b_x4<1>(sfa_t, ptx::sf_chunk_desc(smem + C::kOffSFA + s * 512));
           const uint64_t b_desc = ptx::kmajor_sw128_desc(smem + C::kOffA + s * C::kABytes);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            ptx::mma_mxf8f6f4<1>(d_t, a_desc + 2 * j, b_desc + 2 * j, ptx::with_scale_id(C::kIdesc, j),
-                                 sf_t | (static_cast<uint32_t>(j) << 30),
-                                 (sf_t + 4) | (static_cast<uint32_t>(j) << 30),
-                                 (kb != kb0 || j != 0) ? 1u : 0u);
+          for (int t = 0; t < kTiles; ++t) {
+            const uint64_t a_desc = ptx::kmajor_sw128_desc(smem + C::kOffB + s * C::kBBytes + t * 128 * 128);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              ptx::mma_mxf8f6f4<1>(d_t + t * kNPad, a_desc + 2 * j, b_desc + 2 * j, ptx::with_scale_id(C::kIdesc, j),
+                                   (sf_t + 4 * t) | (static_cast<uint32_t>(j) << 30),
+                                   sfa_t | (static_cast<uint32_t>(j) << 30), (kb != kb0 || j != 0) ? 1u : 0u);
+            }
           }
           ptx::tc_commit<1>(empty_bar(s));
         }
@@ -241,45 +261,51 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t tid = threadIdx.x;  // 0..127: row of the B tile = column of D
     int seg = 0;
     while (walk.next(args, tile, kb0, kb1)) {
-      const int buf = seg & 1;
-      if (!ptx::mbar_wait(acc_full_bar(buf), (seg >> 1) & 1, status, kDevTimeoutEpilogue)) break;
+      const int buf = seg % C::kAccBufs, use = seg / C::kAccBufs;
+      if (!ptx::mbar_wait(acc_full_bar(buf), use & 1, status, kDevTimeoutEpilogue)) break;
       ptx::tc_fence_after();
       const uint32_t acc = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) +
                            static_cast<uint32_t>(buf ? C::kAcc1Col : 0);
       const bool whole = kb0 == 0 && kb1 == args.num_k_blocks;
-      const int n = tile * 128 + static_cast<int>(tid);
+      if (!whole && kTiles != 1) atomicCAS(status, 0, kDevBadTile);  // the host never splits double tiles
+      const int n = tile * kTiles * 128 + static_cast<int>(tid);
       float* part = nullptr;
       if (!whole) {
         const int s = (tile == first_tile) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
         part = args.partials + static_cast<size_t>(s) * kNPad * 128;
       }
 #pragma unroll 1
-      for (int c = 0; c < kNPad; c += 16) {
-        uint32_t v[16];
-        ptx::tmem_ld_32x32b_x16(acc + c, v);
-        ptx::tmem_wait_ld();
-        if (whole) {
-          if (n < args.N) {
+      for (int t = 0; t < kTiles; ++t) {
+        const int nt = n + t * 128;
+#pragma unroll 1
+        for (int c = 0; c < kNPad; c += 16) {
+          uint32_t v[16];
+          ptx::tmem_ld_32x32b_x16(acc + t * kNPad + c, v);
+          ptx::tmem_wait_ld();
+          if (whole) {
+            if (nt < args.N) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if (c + j < args.M)
-                args.d[static_cast<long long>(c + j) * args.ldd + n] = __float2bfloat16_rn(__uint_as_float(v[j]));
+              for (int j = 0; j < 16; ++j) {
+                if (c + j < args.M)
+                  args.d[static_cast<long long>(c + j) * args.ldd + nt] = __float2bfloat16_rn(__uint_as_float(v[j]));
+              }
             }
-          }
-        } else {
-          // Slot layout [kNPad / 4][128 rows][4 columns]: one 16-byte store per
-          // thread and column group, 512 contiguous bytes per warp.
-          float4* part4 = reinterpret_cast<float4*>(part);
+          } else if (kTiles == 1) {
+            // Slot layout [kNPad / 4][128 rows][4 columns]: one 16-byte store per
+            // thread and column group, 512 contiguous bytes per warp.
+            float4* part4 = reinterpret_cast<float4*>(part);
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            part4[(c / 4 + q) * 128 + tid] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                                                         __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+            for (int q = 0; q < 4; ++q)
+              part4[(c / 4 + q) * 128 + tid] =
+                  make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
+                              __uint_as_float(v[4 * q + 3]));
+          }
         }
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(acc_empty_bar(buf));
-      if (!whole) {
+      if (!whole && kTiles == 1) {
         // Publish the partial, count arrivals; the last contributor reduces.
         __threadfence();
         ptx::named_barrier(1, 128);

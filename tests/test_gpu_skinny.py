@@ -74,6 +74,19 @@ def test_split_modes_agree_bitwise():
         outs[split] = o1
 
 
+@pytest.mark.parametrize("shape", [(128, 1280, 1024), (64, 1296, 512), (100, 2064, 768), (33, 512, 256),
+                                   (128, 256, 4096), (128, 144, 384)], ids=str)
+def test_double_b_tiles(shape):
+    # tile_n = 256: two 128-row B tiles per CTA tile share each A stage (whole tiles);
+    # ragged N leaves the second tile of the last pair partly or wholly past N.
+    M, N, K = shape
+    a, sfa, b, sfb = make_operands(M, N, K, seed=M + N)
+    for grid in (0, 2):
+        cfg = GemmConfig(kernel=SKINNY, tile_n=256, split_k=1, max_ctas=grid)
+        assert query(M, N, K, cfg)["tile_n"] == 256
+        _ok(check(run_gemm(a, sfa, b, sfb, M, N, K, cfg), a, sfa, b, sfb, M, N, K))
+
+
 def test_whole_tile_mode():
     M, N, K = 128, 1280, 1024
     a, sfa, b, sfb = make_operands(M, N, K, seed=4)
