@@ -104,6 +104,7 @@ SIGNATURES = {
         [_vp] * 10 + [_i64, _i64, _i64, ctypes.POINTER(GemmConfigC), _i32, _vp, _i64, _vp],
     ),
     "cutex_mxfp8_quantize": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "cutex_mxfp8_quantize_columnwise": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
     "cutex_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "cutex_last_device_status": (ctypes.c_int, [_vp]),
     "cutex_device_sm_count": (ctypes.c_int, [ctypes.POINTER(_i32)]),

@@ -110,4 +110,120 @@ inline bool launch_quantize(const void* x, int dtype, int64_t rows, int64_t K, i
   return cudaGetLastError() == cudaSuccess;
 }
 
+// Columnwise quantiser: the operand layout a GEMM needs when the reduction
+// runs over the rows of x (weight gradients reduce over tokens; input
+// gradients read W along its columns). For x[rows, cols] it writes
+// qt[cols, rows] = quantise(x^T): 1x32 blocks run down the columns of x, and
+// the scales land in the 128x4 swizzled layout of a [cols, K = rows] operand.
+// Same per-block rule as the rowwise kernel.
+//
+// A CTA stages a 128-row x 64-column tile of x in shared memory (coalesced
+// 16/32-byte loads along the rows), then warp w quantises block w % 4 (rows
+// 32b..32b+31) of columns 32 (w / 4) .. + 31: one lane per column, so each
+// lane holds a whole 32-element block (no shuffles) and writes 32 contiguous
+// bytes of qt and one scale byte. Columns from cols up to the next multiple of
+// 128 (the scale layout's padding rows) get scale 0x00 and no element writes.
+constexpr int kColTileRows = 128;
+constexpr int kColTileCols = 64;
+
+template <int kDtype>  // 0: float32, 1: bfloat16
+__global__ void __launch_bounds__(256) mxfp8_quantize_columnwise_kernel(const void* __restrict__ x, int64_t rows,
+                                                                        int64_t cols, int64_t ldx,
+                                                                        uint8_t* __restrict__ qt,
+                                                                        uint8_t* __restrict__ sft) {
+  __shared__ float tile[kColTileRows][kColTileCols + 1];
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kColTileCols;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kColTileRows;
+  const int t = threadIdx.x;
+  // Load: 8 consecutive columns per thread, 8 threads per row, 32 rows per pass.
+  const int lc = (t & 7) * 8;
+#pragma unroll
+  for (int pass = 0; pass < 4; ++pass) {
+    const int lr = pass * 32 + (t >> 3);
+    const int64_t c = c0 + lc;
+    float v[8];
+    if (c + 8 <= cols) {
+      if constexpr (kDtype == 0) {
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + (r0 + lr) * ldx + c);
+        const float4 a = __ldcs(p);
+        const float4 b = __ldcs(p + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+        const uint4 a = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) +
+                                                             (r0 + lr) * ldx + c));
+        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[2 * j] = __uint_as_float(w[j] << 16);
+          v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float e = 0.f;
+        if (c + j < cols) {
+          if constexpr (kDtype == 0) {
+            e = static_cast<const float*>(x)[(r0 + lr) * ldx + c + j];
+          } else {
+            const uint16_t h = reinterpret_cast<const uint16_t*>(x)[(r0 + lr) * ldx + c + j];
+            e = __uint_as_float(static_cast<uint32_t>(h) << 16);
+          }
+        }
+        v[j] = e;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tile[lr][lc + j] = v[j];
+  }
+  __syncthreads();
+  const int warp = t >> 5, lane = t & 31;
+  const int blk = warp & 3;                          // 32-row block of the tile
+  const int lcol = (warp >> 2) * 32 + lane;          // column within the tile
+  const int64_t c = c0 + lcol;                       // output row of qt
+  float v[32];
+  float amax = 0.f;
+  uint32_t nonfinite = 0;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = tile[blk * 32 + i][lcol];
+    const uint32_t bits = __float_as_uint(v[i]) & 0x7FFFFFFFu;
+    nonfinite |= bits >= 0x7F800000u ? 1u : 0u;
+    amax = fmaxf(amax, __uint_as_float(bits));
+  }
+  const uint32_t exp_field = __float_as_uint(amax) >> 23;
+  const uint32_t sbyte = nonfinite ? 0xFFu : (exp_field >= 8u ? exp_field - 8u : 0u);
+  const int64_t cols_pad = (cols + 127) & ~int64_t{127};
+  if (c < cols) {
+    uint32_t w[8];
+    if (!nonfinite) {
+      const float mult = __uint_as_float((254u - sbyte) << 23);  // 2^(127 - sbyte), exact
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        w[j] = fp8x2(v[4 * j] * mult, v[4 * j + 1] * mult) | (fp8x2(v[4 * j + 2] * mult, v[4 * j + 3] * mult) << 16);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = 0u;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(qt + c * rows + r0 + blk * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+  if (c < cols_pad) sft[sf_offset(c, (r0 >> 5) + blk, rows)] = static_cast<uint8_t>(c < cols ? sbyte : 0u);
+}
+
+inline bool launch_quantize_columnwise(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx, void* qt,
+                                       void* sft, cudaStream_t stream) {
+  const int64_t cols_pad = (cols + 127) & ~int64_t{127};
+  const dim3 grid(static_cast<unsigned>(cols_pad / kColTileCols), static_cast<unsigned>(rows / kColTileRows));
+  if (dtype == 0)
+    mxfp8_quantize_columnwise_kernel<0><<<grid, 256, 0, stream>>>(x, rows, cols, ldx, static_cast<uint8_t*>(qt),
+                                                                  static_cast<uint8_t*>(sft));
+  else
+    mxfp8_quantize_columnwise_kernel<1><<<grid, 256, 0, stream>>>(x, rows, cols, ldx, static_cast<uint8_t*>(qt),
+                                                                  static_cast<uint8_t*>(sft));
+  return cudaGetLastError() == cudaSuccess;
+}
+
 }  // namespace cutex

@@ -3,7 +3,7 @@
 from . import dense_gemm_contract
 from .dense_gemm import (GemmConfig, HostGemm, PreparedGemm, dense_gemm, dense_gemm_host, dense_gemm_v13,
                          mxfp8_gemm_launch, query)
-from .quantize import quantize_mxfp8
+from .quantize import quantize_mxfp8, quantize_mxfp8_columnwise
 
 __all__ = [
     "GemmConfig",
@@ -15,5 +15,6 @@ __all__ = [
     "dense_gemm_v13",
     "mxfp8_gemm_launch",
     "quantize_mxfp8",
+    "quantize_mxfp8_columnwise",
     "query",
 ]

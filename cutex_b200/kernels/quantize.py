@@ -47,4 +47,41 @@ def quantize_mxfp8(x, q=None, sf=None, stream=None):
     return q, sf
 
 
-__all__ = ["SF_VECTOR_SIZE", "quantize_mxfp8"]
+def quantize_mxfp8_columnwise(x, qt=None, sft=None, stream=None):
+    """Quantise ``x`` [rows, cols] along its columns -> (qt uint8 [cols, rows], sft uint8 flat).
+
+    ``qt`` = quantise(x^T): the K-major operand (K = rows) of a GEMM that
+    reduces over the rows of ``x`` (weight and input gradients), scales in the
+    128x4 swizzled layout of a [cols, rows] operand. ``rows`` must be a
+    multiple of 128. Runs asynchronously on ``stream``.
+    """
+
+    import torch
+
+    if not x.is_cuda or x.dim() != 2:
+        raise ValueError("x must be a 2-D CUDA tensor")
+    if x.dtype == torch.float32:
+        dtype_code = 0
+    elif x.dtype == torch.bfloat16:
+        dtype_code = 1
+    else:
+        raise TypeError(f"x must be float32 or bfloat16; got {x.dtype}")
+    if x.stride(1) != 1:
+        raise ValueError("x must have unit column stride")
+    rows, cols = x.shape
+    if rows % 128:
+        raise ValueError(f"rows (the GEMM's K) must be a multiple of 128; got {rows}")
+    if qt is None:
+        qt = torch.empty((cols, rows), dtype=torch.uint8, device=x.device)
+    if sft is None:
+        sft = torch.empty(scale_buffer_bytes(cols, rows), dtype=torch.uint8, device=x.device)
+    if qt.numel() * qt.element_size() < rows * cols or sft.numel() * sft.element_size() < scale_buffer_bytes(cols, rows):
+        raise ValueError("output buffers too small")
+    status = _lib.load().cutex_mxfp8_quantize_columnwise(
+        x.data_ptr(), dtype_code, rows, cols, x.stride(0), qt.data_ptr(), sft.data_ptr(), _stream_handle(stream)
+    )
+    _lib.check(status, "cutex_mxfp8_quantize_columnwise")
+    return qt, sft
+
+
+__all__ = ["SF_VECTOR_SIZE", "quantize_mxfp8", "quantize_mxfp8_columnwise"]

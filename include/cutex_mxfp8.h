@@ -173,6 +173,23 @@ CUTEX_API int cutex_mxfp8_quantize(const void* x, int32_t x_dtype, int64_t rows,
                          void* q, void* sf, cutex_stream_t stream);
 
 /*
+ * Columnwise MXFP8 quantiser: for x[rows, cols] (row stride ldx elements)
+ * writes qt[cols, rows] = quantise(x^T) (row stride rows bytes) with the same
+ * per-block rule as cutex_mxfp8_quantize, the 1x32 blocks running down the
+ * columns of x, and the scales in the 128x4 swizzled layout of a [cols, K =
+ * rows] operand (ceil(cols/128)*128*rows/32 bytes; padding rows 0x00). qt is
+ * the K-major operand of a GEMM that reduces over the rows of x: weight
+ * gradients (dW = dY^T X from columnwise dY and X) and input gradients
+ * (dX = dY W from rowwise dY and columnwise W). x_dtype: 0 = float32,
+ * 1 = bfloat16. rows % 128 == 0, ldx % 8 == 0, ldx >= cols.
+ * Replaces Transformer Engine's MXFP8Quantizer(columnwise=True) data for the
+ * Dgrad/Wgrad layouts (no GEMM in the reference consumes them; its contract is
+ * rowwise Fprop only, cutex/kernels/dense_gemm_contract.py:16-22).
+ */
+CUTEX_API int cutex_mxfp8_quantize_columnwise(const void* x, int32_t x_dtype, int64_t rows, int64_t cols,
+                                              int64_t ldx, void* qt, void* sft, cutex_stream_t stream);
+
+/*
  * MXFP8 GEMM for M <= 128 that allocates nothing and takes no workspace.
  * No counterpart in the reference. For callers that cannot call cudaMalloc at
  * launch time (memory-capped pools, allocators that forbid out-of-band

@@ -137,3 +137,15 @@ def test_host_gemm_argument_checks_without_a_device():
         HostGemm(256, 256, 128, blocks=17)
     with pytest.raises(ValueError):
         HostGemm(256, 250, 128)  # N not a multiple of 16
+
+
+def test_columnwise_quantiser_rejects_bad_shapes_without_launching():
+    lib = _lib.load()
+    dummy = 256  # 16-byte aligned placeholder: every case is rejected before any launch
+    assert lib.cutex_mxfp8_quantize_columnwise(dummy, 1, 100, 64, 64, dummy, dummy, None) == _lib.CUTEX_ERR_ALIGN
+    assert lib.cutex_mxfp8_quantize_columnwise(dummy, 1, 128, 64, 60, dummy, dummy, None) == _lib.CUTEX_ERR_ALIGN
+    assert lib.cutex_mxfp8_quantize_columnwise(dummy, 2, 128, 64, 64, dummy, dummy, None) == (
+        _lib.CUTEX_ERR_INVALID_ARGUMENT)
+    assert lib.cutex_mxfp8_quantize_columnwise(None, 1, 128, 64, 64, dummy, dummy, None) == (
+        _lib.CUTEX_ERR_INVALID_ARGUMENT)
+    assert lib.cutex_mxfp8_quantize_columnwise(dummy, 1, 0, 64, 64, dummy, dummy, None) == _lib.CUTEX_ERR_SHAPE
