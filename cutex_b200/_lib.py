@@ -64,6 +64,22 @@ class GemmInfoC(ctypes.Structure):
     ]
 
 
+class EpilogueC(ctypes.Structure):
+    """``cutex_epilogue``: D = alpha * acc + beta * C + bias, BF16 or E4M3 (+ scales) out."""
+
+    _fields_ = [
+        ("alpha", ctypes.c_float),
+        ("beta", ctypes.c_float),
+        ("c", ctypes.c_void_p),
+        ("ldc", ctypes.c_int64),
+        ("bias", ctypes.c_void_p),
+        ("out_dtype", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("d_scales", ctypes.c_void_p),
+        ("reserved", ctypes.c_int64 * 4),
+    ]
+
+
 class CutexError(RuntimeError):
     """A non-zero cutex_status returned by the native library."""
 
@@ -88,6 +104,11 @@ SIGNATURES = {
     "cutex_mxfp8_gemm": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.POINTER(GemmConfigC), _vp, _i64, _vp],
+    ),
+    "cutex_mxfp8_gemm_ex": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.POINTER(GemmConfigC), ctypes.POINTER(EpilogueC),
+         _vp, _i64, _vp],
     ),
     "cutex_mxfp8_query": (
         ctypes.c_int,

@@ -111,6 +111,15 @@ bool encode_output(CUtensorMap* map, void* p, int64_t M, int64_t N, int64_t ldd)
                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
 }
 
+// e4m3 output [M, N] with row stride ldd bytes, 32 x 64 boxes, 64-byte swizzle.
+bool encode_output_fp8(CUtensorMap* map, void* p, int64_t M, int64_t N, int64_t ldd) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ldd)};
+  const uint32_t box[2] = {64u, 32u};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B,
+                CU_TENSOR_MAP_L2_PROMOTION_NONE);
+}
+
 // ------------------------------------------------------------ kernel registry
 
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap,
@@ -119,13 +128,15 @@ using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CU
 struct Variant {
   int cta_group, tile_n, stages, epi_bufs, sf_bufs, dynamic, smem_bytes;
   const void* fn;
-  const void* fn_trace;  // instrumented twin (cutex_mxfp8_gemm_trace), or null
+  const void* fn_trace;   // instrumented twin (cutex_mxfp8_gemm_trace), or null
+  const void* fn_epi[3];  // fused-epilogue twins: [1] BF16 out, [2] E4M3 + scales out; or null
   bool attr_set_trace[kMaxDevices];
   bool attr_set[kMaxDevices];
+  bool attr_set_epi[3][kMaxDevices];
   int max_clusters[kMaxDevices];
 };
 
-template <int CG, int BN, int S, int E, int F, bool D, bool T = false>
+template <int CG, int BN, int S, int E, int F, bool D, bool T = false, bool X = false>
 Variant make_variant() {
   Variant v{};
   v.cta_group = CG;
@@ -137,6 +148,9 @@ Variant make_variant() {
   v.smem_bytes = GemmCfg<CG, BN, S, E, F>::kSmemBytes;
   v.fn = reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D>);
   v.fn_trace = T ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, true>) : nullptr;
+  v.fn_epi[0] = nullptr;
+  v.fn_epi[1] = X ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, false, 1>) : nullptr;
+  v.fn_epi[2] = X ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, false, 2>) : nullptr;
   return v;
 }
 
@@ -144,11 +158,11 @@ Variant make_variant() {
 // dynamic CLC scheduler, [instrumented twin]).
 Variant g_variants[] = {
     // dynamic (cluster launch control) scheduling: the default
-    make_variant<2, 256, 6, 1, 1, true, true>(), make_variant<2, 256, 5, 2, 1, true>(),
+    make_variant<2, 256, 6, 1, 1, true, true, true>(), make_variant<2, 256, 5, 2, 1, true>(),
     make_variant<2, 256, 6, 1, 2, true>(), make_variant<2, 256, 4, 2, 1, true>(),
     make_variant<2, 128, 6, 2, 1, true>(), make_variant<2, 128, 8, 1, 1, true>(),
-    make_variant<1, 256, 4, 1, 1, true, true>(), make_variant<1, 256, 3, 2, 1, true>(),
-    make_variant<1, 128, 6, 1, 1, true>(), make_variant<1, 128, 5, 2, 1, true>(),
+    make_variant<1, 256, 4, 1, 1, true, true, true>(), make_variant<1, 256, 3, 2, 1, true>(),
+    make_variant<1, 128, 6, 1, 1, true, false, true>(), make_variant<1, 128, 5, 2, 1, true>(),
     // static persistent scheduling
     make_variant<1, 128, 4, 2, 2, false>(), make_variant<1, 128, 5, 2, 2, false>(),
     make_variant<1, 128, 6, 1, 2, false>(), make_variant<1, 128, 6, 1, 1, false>(),
@@ -345,20 +359,23 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const void* sfa,
                 const void* sfb, void* d, int64_t M, int64_t N, int64_t K, int64_t ldd,
-                cudaStream_t stream, unsigned long long* trace = nullptr, int trace_cap = 0) {
+                cudaStream_t stream, unsigned long long* trace = nullptr, int trace_cap = 0,
+                const cutex_epilogue* epi = nullptr) {
   Variant* v = plan.variant;
   const bool traced = trace != nullptr;
   if (traced && v->fn_trace == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
-  const void* fn = traced ? v->fn_trace : v->fn;
+  const int epi_kind = epi == nullptr ? 0 : (epi->out_dtype == 1 ? 2 : 1);
+  if (epi_kind != 0 && (traced || v->fn_epi[epi_kind] == nullptr)) return CUTEX_ERR_INVALID_ARGUMENT;
+  const void* fn = traced ? v->fn_trace : (epi_kind != 0 ? v->fn_epi[epi_kind] : v->fn);
   const int cg = v->cta_group;
   CUtensorMap ta, tb, tsa, tsb, td;
+  const bool out_ok = epi_kind == 2 ? encode_output_fp8(&td, d, M, N, ldd) : encode_output(&td, d, M, N, ldd);
   if (!encode_operand(&ta, a, M, K, 128) || !encode_operand(&tb, b, N, K, v->tile_n / cg) ||
-      !encode_scales(&tsa, sfa, M, K, 1) || !encode_scales(&tsb, sfb, N, K, v->tile_n / 128) ||
-      !encode_output(&td, d, M, N, ldd))
+      !encode_scales(&tsa, sfa, M, K, 1) || !encode_scales(&tsb, sfb, N, K, v->tile_n / 128) || !out_ok)
     return CUTEX_ERR_CUDA;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    bool& set = traced ? v->attr_set_trace[dev] : v->attr_set[dev];
+    bool& set = traced ? v->attr_set_trace[dev] : (epi_kind != 0 ? v->attr_set_epi[epi_kind][dev] : v->attr_set[dev]);
     if (!set) {
       if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v->smem_bytes) !=
           cudaSuccess)
@@ -375,6 +392,18 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
   args.raster_along_n = plan.raster_along_n;
   args.trace = trace;
   args.trace_cap = trace_cap;
+  args.alpha = 1.0f;
+  args.beta = 0.0f;
+  args.M = static_cast<int>(M);
+  args.N = static_cast<int>(N);
+  if (epi != nullptr) {
+    args.alpha = epi->alpha;
+    args.beta = epi->beta;
+    args.c = static_cast<const __nv_bfloat16*>(epi->c);
+    args.ldc = epi->ldc;
+    args.bias = static_cast<const __nv_bfloat16*>(epi->bias);
+    args.d_scales = static_cast<uint8_t*>(epi->d_scales);
+  }
 
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(static_cast<unsigned>(plan.grid_ctas), 1, 1);
@@ -537,6 +566,53 @@ extern "C" int cutex_mxfp8_gemm(const void* a, const void* b, const void* sfa, c
   }
   return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd,
                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cutex_mxfp8_gemm_ex(const void* a, const void* b, const void* sfa, const void* sfb, void* d,
+                                   int64_t M, int64_t N, int64_t K, int64_t ldd, const cutex_gemm_config* cfg,
+                                   const cutex_epilogue* epi, void* workspace, int64_t workspace_bytes,
+                                   cutex_stream_t stream) {
+  if (epi == nullptr) return cutex_mxfp8_gemm(a, b, sfa, sfb, d, M, N, K, ldd, cfg, workspace, workspace_bytes, stream);
+  if (a == nullptr || b == nullptr || sfa == nullptr || sfb == nullptr || d == nullptr)
+    return CUTEX_ERR_INVALID_ARGUMENT;
+  if (epi->out_dtype != 0 && epi->out_dtype != 1) return CUTEX_ERR_INVALID_ARGUMENT;
+  if (epi->reserved0 != 0) return CUTEX_ERR_INVALID_ARGUMENT;
+  for (int64_t r : epi->reserved)
+    if (r != 0) return CUTEX_ERR_INVALID_ARGUMENT;
+  int st = validate_shape(M, N, K);
+  if (st != CUTEX_OK) return st;
+  if (M > 0x7FFFFFFF - 256) return CUTEX_ERR_SHAPE;  // the kernel indexes rows as int
+  if (!aligned16(a) || !aligned16(b) || !aligned16(sfa) || !aligned16(sfb) || !aligned16(d))
+    return CUTEX_ERR_ALIGN;
+  if (epi->out_dtype == 0) {
+    if (ldd < N || ldd % 8 != 0 || ldd > kMaxDim) return CUTEX_ERR_ALIGN;
+  } else {
+    // e4m3 D (ldd in bytes) and its scales: whole 128-column scale atoms along N.
+    if (epi->d_scales == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+    if (N % 128 != 0 || ldd < N || ldd % 16 != 0 || ldd > kMaxDim || !aligned16(epi->d_scales))
+      return CUTEX_ERR_ALIGN;
+  }
+  if (epi->bias != nullptr && !aligned16(epi->bias)) return CUTEX_ERR_ALIGN;
+  if (epi->c != nullptr && epi->beta != 0.0f &&
+      (!aligned16(epi->c) || epi->ldc < N || epi->ldc % 8 != 0 || epi->ldc > kMaxDim))
+    return CUTEX_ERR_ALIGN;
+  DeviceState* ds = nullptr;
+  st = current_device_state(&ds);
+  if (st != CUTEX_OK) return st;
+  // The fused builds are large-tile kernels only: route AUTO away from the
+  // skinny kernel, reject an explicit skinny request.
+  cutex_gemm_config c2 = cfg != nullptr ? *cfg : cutex_gemm_config{};
+  if (c2.kernel == CUTEX_KERNEL_SKINNY) return CUTEX_ERR_INVALID_ARGUMENT;
+  if (c2.kernel == CUTEX_KERNEL_AUTO) c2.kernel = (N % 256 == 0 && M > 128) ? CUTEX_KERNEL_2CTA : CUTEX_KERNEL_1CTA;
+  Plan plan{};
+  st = resolve_plan(&c2, M, N, K, ds->sm_count, &plan);
+  if (st != CUTEX_OK) return st;
+  if (plan.variant == nullptr || plan.variant->fn_epi[epi->out_dtype == 1 ? 2 : 1] == nullptr)
+    return CUTEX_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
+  return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd, reinterpret_cast<cudaStream_t>(stream), nullptr, 0,
+                     epi);
 }
 
 extern "C" int cutex_mxfp8_gemm_trace(const void* a, const void* b, const void* sfa,

@@ -33,7 +33,9 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 
+#include "mxfp8_quant.cuh"  // sf_offset: the 128x4 scale layout
 #include "ptx.cuh"
 
 namespace cutex {
@@ -61,6 +63,15 @@ struct GemmArgs {
   int raster_along_n;
   unsigned long long* trace;  // traced builds only: event buffer (see Tracer)
   int trace_cap;              // events per (CTA, role) region
+  // Fused-epilogue builds (kEpi > 0): D = alpha * acc + beta * C + bias[col],
+  // then BF16 (kEpi = 1) or E4M3 with E8M0 scales per 1x32 block along N
+  // (kEpi = 2; scales in the 128x4 swizzled layout of an [M, K = N] operand).
+  float alpha, beta;
+  const __nv_bfloat16* c;  // [M, N] bf16, row stride ldc (elements), or null
+  long long ldc;
+  const __nv_bfloat16* bias;  // [N] bf16 or null
+  uint8_t* d_scales;          // kEpi = 2
+  int M, N;
 };
 
 // In-kernel event trace of the first CTA (pair): each role's recording thread
@@ -235,6 +246,70 @@ __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// alpha * acc + beta * C[row, n0 + j] + bias[n0 + j] on one row's 64
+// accumulator columns (fp32 bits, columns 0-31 in v0, 32-63 in v1). N is a
+// multiple of 16, so each 8-column group is wholly inside or outside D.
+__device__ __forceinline__ void epilogue_affine(uint32_t (&v0)[32], uint32_t (&v1)[32], const GemmArgs& a, int row,
+                                                int n0) {
+  const float alpha = a.alpha;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    v0[j] = __float_as_uint(__uint_as_float(v0[j]) * alpha);
+    v1[j] = __float_as_uint(__uint_as_float(v1[j]) * alpha);
+  }
+  const bool use_c = a.c != nullptr && a.beta != 0.f && row < a.M;
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    if (n0 + 8 * g >= a.N) break;
+    uint32_t* v = g < 4 ? &v0[8 * g] : &v1[8 * (g - 4)];
+    if (use_c) {
+      const uint4 cv = __ldcs(reinterpret_cast<const uint4*>(a.c + static_cast<long long>(row) * a.ldc + n0 + 8 * g));
+      const uint32_t w[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v[2 * q] = __float_as_uint(fmaf(a.beta, __uint_as_float(w[q] << 16), __uint_as_float(v[2 * q])));
+        v[2 * q + 1] = __float_as_uint(fmaf(a.beta, __uint_as_float(w[q] & 0xFFFF0000u), __uint_as_float(v[2 * q + 1])));
+      }
+    }
+    if (a.bias != nullptr) {
+      const uint4 bv = __ldg(reinterpret_cast<const uint4*>(a.bias + n0 + 8 * g));
+      const uint32_t w[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v[2 * q] = __float_as_uint(__uint_as_float(v[2 * q]) + __uint_as_float(w[q] << 16));
+        v[2 * q + 1] = __float_as_uint(__uint_as_float(v[2 * q + 1]) + __uint_as_float(w[q] & 0xFFFF0000u));
+      }
+    }
+  }
+}
+
+// One 1x32 block (fp32 bits) -> 8 words of E4M3 codes + the E8M0 scale byte,
+// with the quantiser's rule (scale exponent floor(log2 amax) - 8, 0x00 for an
+// all-zero block, 0xFF and zero codes for a block holding a non-finite value).
+__device__ __forceinline__ uint32_t quantize_block32(const uint32_t (&v)[32], uint32_t (&w)[8]) {
+  float amax = 0.f;
+  uint32_t nonfinite = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const uint32_t bits = v[j] & 0x7FFFFFFFu;
+    nonfinite |= bits >= 0x7F800000u ? 1u : 0u;
+    amax = fmaxf(amax, __uint_as_float(bits));
+  }
+  const uint32_t exp_field = __float_as_uint(amax) >> 23;
+  const uint32_t sbyte = nonfinite ? 0xFFu : (exp_field >= 8u ? exp_field - 8u : 0u);
+  const float mult = __uint_as_float((254u - (nonfinite ? 127u : sbyte)) << 23);  // 2^(127 - sbyte), exact
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint32_t lo = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(
+        make_float2(__uint_as_float(v[4 * q]) * mult, __uint_as_float(v[4 * q + 1]) * mult), __NV_SATFINITE, __NV_E4M3));
+    const uint32_t hi = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(
+        make_float2(__uint_as_float(v[4 * q + 2]) * mult, __uint_as_float(v[4 * q + 3]) * mult), __NV_SATFINITE,
+        __NV_E4M3));
+    w[q] = nonfinite ? 0u : (lo | (hi << 16));
+  }
+  return sbyte;
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
@@ -306,7 +381,7 @@ __device__ __forceinline__ void settle_inflight_copies() {
 }
 
 template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs, int kSFBufs, bool kDynamic,
-          bool kTrace = false>
+          bool kTrace = false, int kEpi = 0>
 __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
     mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -597,17 +672,39 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
           tr.rec_at(kEvEpiRelease, t_rel, t, 0);
         }
         const uint32_t slot = chunk_ctr % kEpiBufs;
+        if constexpr (kEpi != 0) epilogue_affine(v0, v1, args, m_row + static_cast<int>(lane), n_col + c * 64);
         if (chunk_ctr >= static_cast<uint32_t>(kEpiBufs)) {
           if (lane == 0) ptx::bulk_wait_group_read<kEpiBufs - 1>();
           __syncwarp();
         }
-        const uint32_t row_addr = cbuf + slot * C::kCBufBytes + lane * 128u;
+        if constexpr (kEpi == 2) {
+          // E4M3 row of 64 bytes, 64-byte swizzle (16-byte chunk ^ (row >> 1) & 3),
+          // and the two scale bytes of its 1x32 blocks (one 16-bit store).
+          uint32_t w0[8], w1[8];
+          const uint32_t s0 = quantize_block32(v0, w0);
+          const uint32_t s1 = quantize_block32(v1, w1);
+          const uint32_t row_addr = cbuf + slot * C::kCBufBytes + lane * 64u;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t* src = j < 4 ? &v0[j * 8] : &v1[(j - 4) * 8];
-          st_shared_v4(row_addr + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4),
-                       pack_bf16x2(src[0], src[1]), pack_bf16x2(src[2], src[3]),
-                       pack_bf16x2(src[4], src[5]), pack_bf16x2(src[6], src[7]));
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t* w = q < 2 ? &w0[4 * q] : &w1[4 * (q - 2)];
+            st_shared_v4(row_addr + ((static_cast<uint32_t>(q) ^ ((lane >> 1) & 3u)) << 4), w[0], w[1], w[2], w[3]);
+          }
+          const int row = m_row + static_cast<int>(lane);
+          const int n0 = n_col + c * 64;
+          if (row < ((args.M + 127) & ~127) && n0 < args.N) {
+            const bool real = row < args.M;  // padding rows of the scale layout: 0x00
+            const int64_t off = sf_offset(row, n0 >> 5, args.N);
+            *reinterpret_cast<uint16_t*>(args.d_scales + off) = static_cast<uint16_t>(real ? (s0 | (s1 << 8)) : 0u);
+          }
+        } else {
+          const uint32_t row_addr = cbuf + slot * C::kCBufBytes + lane * 128u;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* src = j < 4 ? &v0[j * 8] : &v1[(j - 4) * 8];
+            st_shared_v4(row_addr + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4),
+                         pack_bf16x2(src[0], src[1]), pack_bf16x2(src[2], src[3]),
+                         pack_bf16x2(src[4], src[5]), pack_bf16x2(src[6], src[7]));
+          }
         }
         ptx::fence_proxy_async_smem();
         __syncwarp();

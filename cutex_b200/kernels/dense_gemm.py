@@ -141,6 +141,54 @@ def dense_gemm(a, b, sfa, sfb, out, stream=None, config: GemmConfig | None = Non
     return out
 
 
+def dense_gemm_fused(a, b, sfa, sfb, out, *, alpha: float = 1.0, beta: float = 0.0, c=None, bias=None,
+                     out_scales=None, stream=None, config: GemmConfig | None = None):
+    """D = alpha * dequant(A) @ dequant(B)^T + beta * C + bias, fused into the GEMM's epilogue.
+
+    ``out`` bf16 [M, N], or E4M3 [M, N] (``torch.float8_e4m3fn`` / ``uint8``) with
+    ``out_scales`` (``scale_buffer_bytes(M, N)`` bytes): the next layer's MXFP8
+    operand, 1x32 blocks along N, quantised with the same rule as
+    ``quantize_mxfp8``. ``c`` bf16 [M, N] (may be ``out`` itself), ``bias`` bf16
+    [N]. Runs the large-tile kernels only (any M).
+    """
+
+    import torch
+
+    for t, name in ((a, "a"), (b, "b"), (sfa, "sfa"), (sfb, "sfb")):
+        _byte_view_ok(t, name)
+    m, k = a.shape
+    n = b.shape[0]
+    validate_mxfp8_gemm_shape(m, n, k)
+    if b.shape[1] != k or not (a.is_contiguous() and b.is_contiguous()):
+        raise ValueError("a [M, K] and b [N, K] must be contiguous with matching K")
+    fp8_out = out.dtype in (torch.uint8, getattr(torch, "float8_e4m3fn", torch.uint8))
+    if tuple(out.shape) != (m, n) or out.stride(1) != 1 or not (fp8_out or out.dtype == torch.bfloat16):
+        raise ValueError(f"out must be a bf16 or e4m3 [{m}, {n}] tensor with unit column stride")
+    epi = _lib.EpilogueC()
+    epi.alpha = float(alpha)
+    epi.beta = float(beta)
+    if c is not None:
+        if c.dtype != torch.bfloat16 or tuple(c.shape) != (m, n) or c.stride(1) != 1:
+            raise ValueError(f"c must be a bf16 [{m}, {n}] tensor with unit column stride")
+        epi.c = c.data_ptr()
+        epi.ldc = c.stride(0)
+    if bias is not None:
+        if bias.dtype != torch.bfloat16 or bias.numel() != n or not bias.is_contiguous():
+            raise ValueError(f"bias must be a contiguous bf16 tensor of {n} elements")
+        epi.bias = bias.data_ptr()
+    if fp8_out:
+        if out_scales is None or out_scales.numel() * out_scales.element_size() < scale_buffer_bytes(m, n):
+            raise ValueError(f"e4m3 output needs out_scales of {scale_buffer_bytes(m, n)} bytes")
+        epi.out_dtype = 1
+        epi.d_scales = out_scales.data_ptr()
+    cfg = (config or GemmConfig()).to_c()
+    status = _lib.load().cutex_mxfp8_gemm_ex(
+        a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), out.data_ptr(), m, n, k, out.stride(0),
+        ctypes.byref(cfg), ctypes.byref(epi), None, 0, _stream_handle(stream))
+    _lib.check(status, "cutex_mxfp8_gemm_ex")
+    return out
+
+
 class PreparedGemm:
     """A GEMM launch with every argument resolved once: calling it is a single C-ABI call.
 
@@ -296,6 +344,7 @@ __all__ = [
     "HostGemm",
     "PreparedGemm",
     "dense_gemm",
+    "dense_gemm_fused",
     "dense_gemm_host",
     "dense_gemm_v13",
     "device_target",

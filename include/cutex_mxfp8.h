@@ -98,6 +98,26 @@ typedef struct cutex_gemm_info {
 } cutex_gemm_info;
 
 /*
+ * Fused epilogue of cutex_mxfp8_gemm_ex:
+ *   D = alpha * (A . B^T) + beta * C + bias[col]
+ * then BF16 (out_dtype 0) or E4M3 with one E8M0 scale per 1x32 block along N
+ * (out_dtype 1: the next layer's MXFP8 operand, same rule as
+ * cutex_mxfp8_quantize, scales in the 128x4 swizzled layout of an
+ * [M, K = N] operand, ceil(M/128)*128*N/32 bytes in d_scales).
+ */
+typedef struct cutex_epilogue {
+  float alpha;            /* 1.0f for none */
+  float beta;             /* 0.0f for none (C is then not read) */
+  const void* c;          /* bf16 [M, N], row stride ldc elements, 16-byte aligned; may equal d */
+  int64_t ldc;            /* ldc >= N, ldc % 8 == 0 */
+  const void* bias;       /* bf16 [N], 16-byte aligned, or NULL */
+  int32_t out_dtype;      /* 0 = bf16 D, 1 = e4m3 D (ldd in bytes, ldd % 16 == 0) + d_scales; N % 128 == 0 */
+  int32_t reserved0;      /* must be 0 */
+  void* d_scales;         /* out_dtype 1: 16-byte aligned */
+  int64_t reserved[4];    /* must be 0 */
+} cutex_epilogue;
+
+/*
  * MXFP8 GEMM, general shape.
  * Replaces the reference's `@cute.jit dense_gemm_vN(a_ptr, b_ptr, sfa_ptr,
  * sfb_ptr, c_ptr[, max_active_clusters], stream)` launch
@@ -120,6 +140,21 @@ CUTEX_API int cutex_mxfp8_gemm(const void* a, const void* b, const void* sfa, co
                      int64_t M, int64_t N, int64_t K, int64_t ldd,
                      const cutex_gemm_config* cfg, void* workspace, int64_t workspace_bytes,
                      cutex_stream_t stream);
+
+/*
+ * cutex_mxfp8_gemm with a fused epilogue (epi may be NULL: plain GEMM). The
+ * fused builds are the default CTA-pair (N % 256 == 0) and single-CTA kernels;
+ * any M (rows beyond M are not written), no skinny kernel. A cfg that names a
+ * tile configuration without a fused build returns CUTEX_ERR_INVALID_ARGUMENT.
+ * With out_dtype 1, d is e4m3 [M, N] with row stride ldd bytes.
+ * No counterpart in the reference (its epilogue is a plain BF16 store,
+ * cutex/kernels/dense_gemm_v13.py:811-914; the C-source metadata it carries is
+ * unused, dense_gemm_v13.py:1133-1142).
+ */
+CUTEX_API int cutex_mxfp8_gemm_ex(const void* a, const void* b, const void* sfa, const void* sfb, void* d,
+                                  int64_t M, int64_t N, int64_t K, int64_t ldd, const cutex_gemm_config* cfg,
+                                  const cutex_epilogue* epi, void* workspace, int64_t workspace_bytes,
+                                  cutex_stream_t stream);
 
 /*
  * Resolve a configuration for a shape without launching anything.

@@ -149,3 +149,27 @@ def test_columnwise_quantiser_rejects_bad_shapes_without_launching():
     assert lib.cutex_mxfp8_quantize_columnwise(None, 1, 128, 64, 64, dummy, dummy, None) == (
         _lib.CUTEX_ERR_INVALID_ARGUMENT)
     assert lib.cutex_mxfp8_quantize_columnwise(dummy, 1, 0, 64, 64, dummy, dummy, None) == _lib.CUTEX_ERR_SHAPE
+
+
+def test_fused_epilogue_argument_checks_without_launching():
+    lib = _lib.load()
+    p = 256  # 16-byte aligned placeholder: every case below is rejected before any launch
+    cfg = _lib.make_config()
+
+    def call(epi, M=256, N=256, K=128, ldd=256):
+        return lib.cutex_mxfp8_gemm_ex(p, p, p, p, p, M, N, K, ldd, ctypes.byref(cfg), ctypes.byref(epi), None, 0,
+                                       None)
+
+    e = _lib.EpilogueC(alpha=1.0, out_dtype=2)
+    assert call(e) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    e = _lib.EpilogueC(alpha=1.0, out_dtype=1)  # e4m3 out without a scale buffer
+    assert call(e) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    e = _lib.EpilogueC(alpha=1.0, out_dtype=1, d_scales=p)
+    assert call(e, N=272, ldd=272) == _lib.CUTEX_ERR_ALIGN  # N % 128 for the scale atoms
+    e = _lib.EpilogueC(alpha=1.0, bias=p + 8)
+    assert call(e) == _lib.CUTEX_ERR_ALIGN
+    e = _lib.EpilogueC(alpha=1.0, beta=1.0, c=p, ldc=100)
+    assert call(e) == _lib.CUTEX_ERR_ALIGN
+    e = _lib.EpilogueC(alpha=1.0)
+    e.reserved[2] = 1
+    assert call(e) == _lib.CUTEX_ERR_INVALID_ARGUMENT
