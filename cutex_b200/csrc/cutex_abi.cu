@@ -19,6 +19,7 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr int64_t kMaxDim = (int64_t{1} << 31) - 1;
+constexpr int kMaxGatherPeers = 7;  // peers of the fused all-gather (8 GPUs per node)
 
 struct DeviceState {
   bool ready = false;
@@ -129,10 +130,10 @@ struct Variant {
   int cta_group, tile_n, stages, epi_bufs, sf_bufs, dynamic, smem_bytes;
   const void* fn;
   const void* fn_trace;   // instrumented twin (cutex_mxfp8_gemm_trace), or null
-  const void* fn_epi[3];  // fused-epilogue twins: [1] BF16 out, [2] E4M3 + scales out; or null
+  const void* fn_epi[4];  // fused-epilogue twins: [1] BF16 out, [2] E4M3 + scales out, [3] all-gather
   bool attr_set_trace[kMaxDevices];
   bool attr_set[kMaxDevices];
-  bool attr_set_epi[3][kMaxDevices];
+  bool attr_set_epi[4][kMaxDevices];
   int max_clusters[kMaxDevices];
 };
 
@@ -151,6 +152,7 @@ Variant make_variant() {
   v.fn_epi[0] = nullptr;
   v.fn_epi[1] = X ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, false, 1>) : nullptr;
   v.fn_epi[2] = X ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, false, 2>) : nullptr;
+  v.fn_epi[3] = X ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, false, 3>) : nullptr;
   return v;
 }
 
@@ -360,11 +362,11 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const void* sfa,
                 const void* sfb, void* d, int64_t M, int64_t N, int64_t K, int64_t ldd,
                 cudaStream_t stream, unsigned long long* trace = nullptr, int trace_cap = 0,
-                const cutex_epilogue* epi = nullptr) {
+                const cutex_epilogue* epi = nullptr, const CUtensorMap* peer_maps = nullptr, int num_peers = 0) {
   Variant* v = plan.variant;
   const bool traced = trace != nullptr;
   if (traced && v->fn_trace == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
-  const int epi_kind = epi == nullptr ? 0 : (epi->out_dtype == 1 ? 2 : 1);
+  const int epi_kind = peer_maps != nullptr ? 3 : (epi == nullptr ? 0 : (epi->out_dtype == 1 ? 2 : 1));
   if (epi_kind != 0 && (traced || v->fn_epi[epi_kind] == nullptr)) return CUTEX_ERR_INVALID_ARGUMENT;
   const void* fn = traced ? v->fn_trace : (epi_kind != 0 ? v->fn_epi[epi_kind] : v->fn);
   const int cg = v->cta_group;
@@ -396,6 +398,8 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
   args.beta = 0.0f;
   args.M = static_cast<int>(M);
   args.N = static_cast<int>(N);
+  args.peer_maps = peer_maps;
+  args.num_peers = num_peers;
   if (epi != nullptr) {
     args.alpha = epi->alpha;
     args.beta = epi->beta;
@@ -613,6 +617,94 @@ extern "C" int cutex_mxfp8_gemm_ex(const void* a, const void* b, const void* sfa
   if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
   return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd, reinterpret_cast<cudaStream_t>(stream), nullptr, 0,
                      epi);
+}
+
+namespace {
+
+PFN_cuMemGetAddressRange_v3020 address_range_fn() {
+  static PFN_cuMemGetAddressRange_v3020 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+  }();
+  return fn;
+}
+
+}  // namespace
+
+extern "C" int cutex_ipc_export(const void* dev_ptr, void* handle, int64_t* offset) {
+  if (dev_ptr == nullptr || handle == nullptr || offset == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  auto range = address_range_fn();
+  if (range == nullptr) return CUTEX_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) return CUTEX_ERR_CUDA;
+  cudaIpcMemHandle_t h{};
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return CUTEX_ERR_CUDA;
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return CUTEX_OK;
+}
+
+extern "C" int cutex_ipc_import(const void* handle, int64_t offset, void** dev_ptr, void** mapping) {
+  if (handle == nullptr || dev_ptr == nullptr || mapping == nullptr || offset < 0) return CUTEX_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h{};
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return CUTEX_ERR_CUDA;
+  *mapping = base;
+  *dev_ptr = static_cast<char*>(base) + offset;
+  return CUTEX_OK;
+}
+
+extern "C" int cutex_ipc_close(void* mapping) {
+  if (mapping == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  return cudaIpcCloseMemHandle(mapping) == cudaSuccess ? CUTEX_OK : CUTEX_ERR_CUDA;
+}
+
+extern "C" int cutex_mxfp8_gemm_allgather(const void* a, const void* b, const void* sfa, const void* sfb, void* d,
+                                          int64_t M, int64_t N, int64_t K, int64_t ldd, const void* const* peer_d,
+                                          int32_t num_peers, void* map_buffer, int64_t map_buffer_bytes,
+                                          const cutex_gemm_config* cfg, cutex_stream_t stream) {
+  if (a == nullptr || b == nullptr || sfa == nullptr || sfb == nullptr || d == nullptr || peer_d == nullptr ||
+      map_buffer == nullptr)
+    return CUTEX_ERR_INVALID_ARGUMENT;
+  if (num_peers < 1 || num_peers > kMaxGatherPeers) return CUTEX_ERR_INVALID_ARGUMENT;
+  if (map_buffer_bytes < static_cast<int64_t>(num_peers) * static_cast<int64_t>(sizeof(CUtensorMap)))
+    return CUTEX_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(map_buffer) & 63u) != 0) return CUTEX_ERR_ALIGN;  // CUtensorMap alignment
+  int st = validate_shape(M, N, K);
+  if (st != CUTEX_OK) return st;
+  if (ldd < N || ldd % 8 != 0 || ldd > kMaxDim) return CUTEX_ERR_ALIGN;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(sfa) || !aligned16(sfb) || !aligned16(d)) return CUTEX_ERR_ALIGN;
+  for (int p = 0; p < num_peers; ++p)
+    if (peer_d[p] == nullptr || !aligned16(peer_d[p])) return CUTEX_ERR_ALIGN;
+  DeviceState* ds = nullptr;
+  st = current_device_state(&ds);
+  if (st != CUTEX_OK) return st;
+  cutex_gemm_config c2 = cfg != nullptr ? *cfg : cutex_gemm_config{};
+  if (c2.kernel == CUTEX_KERNEL_SKINNY) return CUTEX_ERR_INVALID_ARGUMENT;
+  if (c2.kernel == CUTEX_KERNEL_AUTO) c2.kernel = (N % 256 == 0 && M > 128) ? CUTEX_KERNEL_2CTA : CUTEX_KERNEL_1CTA;
+  Plan plan{};
+  st = resolve_plan(&c2, M, N, K, ds->sm_count, &plan);
+  if (st != CUTEX_OK) return st;
+  if (plan.variant == nullptr || plan.variant->fn_epi[3] == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  // The peers' D regions as TMA store descriptors, placed in map_buffer in
+  // stream order (the copy stages the host array before returning).
+  CUtensorMap maps[kMaxGatherPeers];
+  for (int p = 0; p < num_peers; ++p)
+    if (!encode_output(&maps[p], const_cast<void*>(peer_d[p]), M, N, ldd)) return CUTEX_ERR_CUDA;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(map_buffer, maps, sizeof(CUtensorMap) * num_peers, cudaMemcpyHostToDevice, s) != cudaSuccess)
+    return CUTEX_ERR_CUDA;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
+  return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd, s, nullptr, 0, nullptr,
+                     static_cast<const CUtensorMap*>(map_buffer), num_peers);
 }
 
 extern "C" int cutex_mxfp8_gemm_trace(const void* a, const void* b, const void* sfa,

@@ -72,6 +72,11 @@ struct GemmArgs {
   const __nv_bfloat16* bias;  // [N] bf16 or null
   uint8_t* d_scales;          // kEpi = 2
   int M, N;
+  // kEpi = 3 (fused all-gather): every D chunk is also stored, by TMA from the
+  // same staging buffer, through each of num_peers tensor maps (global memory)
+  // that describe the peers' copies of D (NVLink peer memory).
+  const CUtensorMap* peer_maps;
+  int num_peers;
 };
 
 // In-kernel event trace of the first CTA (pair): each role's recording thread
@@ -672,7 +677,8 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
           tr.rec_at(kEvEpiRelease, t_rel, t, 0);
         }
         const uint32_t slot = chunk_ctr % kEpiBufs;
-        if constexpr (kEpi != 0) epilogue_affine(v0, v1, args, m_row + static_cast<int>(lane), n_col + c * 64);
+        if constexpr (kEpi == 1 || kEpi == 2)
+          epilogue_affine(v0, v1, args, m_row + static_cast<int>(lane), n_col + c * 64);
         if (chunk_ctr >= static_cast<uint32_t>(kEpiBufs)) {
           if (lane == 0) ptx::bulk_wait_group_read<kEpiBufs - 1>();
           __syncwarp();
@@ -710,6 +716,10 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
         __syncwarp();
         if (lane == 0) {
           ptx::tma_store_2d(&tmap_d, cbuf + slot * C::kCBufBytes, n_col + c * 64, m_row);
+          if constexpr (kEpi == 3) {
+            for (int p = 0; p < args.num_peers; ++p)
+              ptx::tma_store_2d(args.peer_maps + p, cbuf + slot * C::kCBufBytes, n_col + c * 64, m_row);
+          }
           ptx::bulk_commit_group();
         }
         ++chunk_ctr;

@@ -62,4 +62,84 @@ def allgather_columns(d_local, world: int, group=None):
     return gathered.view(world, m, n_local).permute(1, 0, 2).reshape(m, world * n_local)
 
 
-__all__ = ["SHARD_ALIGN", "Shard", "allgather_columns", "scale_rows_slice", "shard_bounds"]
+class FusedAllGatherGemm:
+    """N-sharded GEMM whose epilogue also writes each finished tile into every peer's full D.
+
+    Every rank holds a full ``d_full`` [M, N] (bf16). Rank r computes
+    ``d_full[:, n0:n1]`` from all of A and its B slice; the kernel stores each
+    finished chunk into its own copy and, over NVLink, into the same place of
+    every peer's copy (``cutex_mxfp8_gemm_allgather``), so the gather overlaps
+    the GEMM. The peer copies are mapped once with CUDA IPC (handles exchanged
+    through ``group``). A call ends with a one-element all-reduce on the
+    current stream; after it every rank's ``d_full`` is complete.
+    """
+
+    def __init__(self, m: int, n: int, k: int, group=None, config=None, device=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+        from .kernels.dense_gemm import GemmConfig
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world < 2 or self.world > 8:
+            raise ValueError("the fused all-gather needs 2..8 ranks on one node")
+        self.shard = shard_bounds(n, self.world, self.rank)
+        self.m, self.n, self.k = m, n, k
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.d_full = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        lib = _lib.load()
+        handle = ctypes.create_string_buffer(64)
+        offset = ctypes.c_int64(0)
+        _lib.check(lib.cutex_ipc_export(self.d_full.data_ptr(), handle, ctypes.byref(offset)), "cutex_ipc_export")
+        entries = [None] * self.world
+        dist.all_gather_object(entries, (handle.raw, offset.value), group=group)
+        self._mappings = []
+        peers = []
+        for r, (h, off) in enumerate(entries):
+            if r == self.rank:
+                continue
+            ptr, mapping = ctypes.c_void_p(), ctypes.c_void_p()
+            _lib.check(lib.cutex_ipc_import(h, off, ctypes.byref(ptr), ctypes.byref(mapping)), "cutex_ipc_import")
+            self._mappings.append(mapping.value)
+            peers.append(ptr.value + self.shard.n0 * 2)  # this rank's columns in peer r's copy
+        self._peers = (ctypes.c_void_p * len(peers))(*peers)
+        self._maps = torch.empty(128 * len(peers), dtype=torch.uint8, device=dev)
+        self._cfg = (config or GemmConfig()).to_c()
+        self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    def __call__(self, a, b_local, sfa, sfb_local, stream=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+        from .kernels.dense_gemm import _stream_handle
+
+        handle = _stream_handle(stream)
+        status = _lib.load().cutex_mxfp8_gemm_allgather(
+            a.data_ptr(), b_local.data_ptr(), sfa.data_ptr(), sfb_local.data_ptr(),
+            self.d_full.data_ptr() + self.shard.n0 * 2, self.m, self.shard.n, self.k, self.n, self._peers,
+            len(self._peers), self._maps.data_ptr(), self._maps.numel(), ctypes.byref(self._cfg), handle)
+        _lib.check(status, "cutex_mxfp8_gemm_allgather")
+        # Cross-rank barrier in stream order: every rank's pushes have landed.
+        s = stream if stream is not None and not isinstance(stream, int) else torch.cuda.current_stream()
+        with torch.cuda.stream(s):
+            dist.all_reduce(self._flag, group=self.group)
+        return self.d_full
+
+    def close(self) -> None:
+        from . import _lib
+
+        lib = _lib.load()
+        for mapping in self._mappings:
+            lib.cutex_ipc_close(mapping)
+        self._mappings = []
+
+
+__all__ = ["SHARD_ALIGN", "FusedAllGatherGemm", "Shard", "allgather_columns", "scale_rows_slice", "shard_bounds"]

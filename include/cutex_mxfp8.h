@@ -157,6 +157,38 @@ CUTEX_API int cutex_mxfp8_gemm_ex(const void* a, const void* b, const void* sfa,
                                   cutex_stream_t stream);
 
 /*
+ * CUDA IPC for the fused all-gather's peer buffers (one process per GPU).
+ * cutex_ipc_export: the 64-byte handle of the device allocation that holds
+ * dev_ptr and dev_ptr's byte offset in it. cutex_ipc_import (another process,
+ * another GPU of the node): maps that allocation, returns the address of the
+ * same byte in *dev_ptr and the mapping to pass to cutex_ipc_close.
+ */
+CUTEX_API int cutex_ipc_export(const void* dev_ptr, void* handle, int64_t* offset);
+CUTEX_API int cutex_ipc_import(const void* handle, int64_t offset, void** dev_ptr, void** mapping);
+CUTEX_API int cutex_ipc_close(void* mapping);
+
+/*
+ * N-sharded GEMM with the all-gather of D fused into the epilogue: computes
+ * this rank's D[:, n0:n0+N] (d points at its first element inside this
+ * rank's full D, row stride ldd) and stores every finished 32 x 64 chunk, by
+ * TMA from the same shared-memory staging buffer, also into each peer's full
+ * D (peer_d[p] = the same element in peer p's copy, mapped with
+ * cutex_ipc_import; 16-byte aligned; num_peers <= 7), so the gather overlaps
+ * the GEMM tile by tile over NVLink. map_buffer: device memory for the peers'
+ * TMA descriptors, >= 128 * num_peers bytes, 64-byte aligned, written on
+ * `stream` before the launch (not capturable into a CUDA graph). The peers'
+ * copies are complete when every rank's call has completed: order readers
+ * after a cross-rank barrier on the stream (e.g. a one-element NCCL
+ * all-reduce). Kernel choice as cutex_mxfp8_gemm_ex (no skinny kernel).
+ * Replaces the GEMM + ncclAllGather + re-layout sequence (one NCCL
+ * collective after the kernel, then a permute).
+ */
+CUTEX_API int cutex_mxfp8_gemm_allgather(const void* a, const void* b, const void* sfa, const void* sfb, void* d,
+                                         int64_t M, int64_t N, int64_t K, int64_t ldd, const void* const* peer_d,
+                                         int32_t num_peers, void* map_buffer, int64_t map_buffer_bytes,
+                                         const cutex_gemm_config* cfg, cutex_stream_t stream);
+
+/*
  * Resolve a configuration for a shape without launching anything.
  * Replaces the host-side resource accounting of dense_gemm_v13
  * (cutex/kernels/dense_gemm_v13.py:1095-1239: SMEM layouts, tma_bytes, grid).
