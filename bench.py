@@ -53,7 +53,8 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--e2e-blocks", type=int, default=4,
                    help="host pipeline: output cut into up to BxB blocks (copies and GEMMs overlapped)")
-    p.add_argument("--allgather", action="store_true", help="also time the NCCL all-gather of D (N > 1)")
+    p.add_argument("--allgather", action="store_true",
+                   help="N > 1: also time gathering D on every rank, NCCL after the GEMM vs fused into it")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--config", type=str, default="", help="native config as JSON, e.g. '{\"kernel\": 2}'")
     p.add_argument("--no-graph", action="store_true", help="plain launches instead of one CUDA graph")
@@ -491,8 +492,35 @@ def bench_cutex(args):
         torch.cuda.synchronize()
         tg = torch.tensor([s3.elapsed_time(e3)], dtype=torch.float64, device=device)
         dist.all_reduce(tg, op=dist.ReduceOp.MAX)
-        allgather = {"ms": float(tg[0]), "bytes_per_rank_received": int(full.numel() * 2 * (world - 1) / world)}
+        allgather = {"nccl_ms": float(tg[0]), "gemm_ms": launch_avg_ms,
+                     "gemm_then_nccl_ms": launch_avg_ms + float(tg[0]),
+                     "bytes_per_rank_received": int(full.numel() * 2 * (world - 1) / world)}
         del full
+        # The same result with the gather fused into the GEMM's epilogue (peer TMA
+        # stores over NVLink) and a one-element all-reduce as the closing barrier.
+        from cutex_b200.sharding import FusedAllGatherGemm
+
+        fused = FusedAllGatherGemm(m, n, k, config=cfg)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                fused(a, b, sfa, sfb, stream=stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        s5, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        with torch.cuda.stream(stream):
+            s5.record(stream)
+            for _ in range(reps):
+                fused(a, b, sfa, sfb, stream=stream)
+            e5.record(stream)
+        torch.cuda.synchronize()
+        tf = torch.tensor([s5.elapsed_time(e5) / reps], dtype=torch.float64, device=device)
+        dist.all_reduce(tf, op=dist.ReduceOp.MAX)
+        allgather["fused_ms"] = float(tf[0])
+        allgather["fused_path"] = "cutex_mxfp8_gemm_allgather + one-element NCCL all-reduce"
+        dist.barrier()
+        fused.close()
+        del fused
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
