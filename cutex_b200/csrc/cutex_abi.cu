@@ -272,8 +272,12 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   if (cfg.tile_n != 0 && cfg.tile_n != 128 && cfg.tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
   int kernel = cfg.kernel;
   if (kernel == CUTEX_KERNEL_AUTO) {
+    // CTA-pair 256x256 tiles when they fill at least one wave of pairs;
+    // below that, single-CTA 128-row tiles give twice the parallelism
+    // (measured 2048^3: 1535 vs 1469 TFLOP/s).
+    const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
     if (M <= 128) kernel = CUTEX_KERNEL_SKINNY;
-    else kernel = (N % 256 == 0) ? CUTEX_KERNEL_2CTA : CUTEX_KERNEL_1CTA;
+    else kernel = (N % 256 == 0 && pair_tiles >= sm_count / 2) ? CUTEX_KERNEL_2CTA : CUTEX_KERNEL_1CTA;
   }
   plan->skinny = nullptr;
   plan->variant = nullptr;
