@@ -5,6 +5,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -20,6 +21,10 @@ namespace {
 constexpr int kMaxDevices = 64;
 constexpr int64_t kMaxDim = (int64_t{1} << 31) - 1;
 constexpr int kMaxGatherPeers = 7;  // peers of the fused all-gather (8 GPUs per node)
+static_assert(sizeof(cutex_epilogue) == 80 && offsetof(cutex_epilogue, out_dtype) == 32 &&
+                  offsetof(cutex_epilogue, d_scales) == 40,
+              "cutex_epilogue layout (mirrored by the Python binding)");
+static_assert(sizeof(cutex_gemm_config) == 64 && sizeof(cutex_gemm_info) == 64, "config / info layouts");
 
 struct DeviceState {
   bool ready = false;

@@ -269,6 +269,83 @@ __global__ void __launch_bounds__(192, 1)
       const bool whole = kb0 == 0 && kb1 == args.num_k_blocks;
       if (!whole && kTiles != 1) atomicCAS(status, 0, kDevBadTile);  // the host never splits double tiles
       const int n = tile * kTiles * 128 + static_cast<int>(tid);
+      // A tile cut between CTAs: the contributors of its K-range and whether all
+      // the others have already published their slots. If so this CTA is the
+      // last: it sums their slots with its own accumulator read straight from
+      // TMEM (no slot of its own, no second pass over global memory), writes D
+      // and resets the counter. The sum runs in contributor order either way,
+      // so the result does not depend on which contributor finishes last.
+      int c0 = 0, c1 = 0;
+      bool early_last = false;
+      if (!whole && kTiles == 1) {
+        const long long t_u0 = static_cast<long long>(tile - args.dp_tiles) * args.num_k_blocks;
+        c0 = static_cast<int>(sk_owner(t_u0, P, U));
+        c1 = static_cast<int>(sk_owner(t_u0 + args.num_k_blocks - 1, P, U));
+        if (tid == 0) {
+          unsigned int done;
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(done) : "l"(args.counters + tile) : "memory");
+          slot[1] = done == static_cast<unsigned int>(c1 - c0) ? 1u : 0u;
+        }
+        ptx::named_barrier(1, 128);
+        early_last = slot[1] != 0u;
+      }
+      auto slot_of = [&](int cc) {
+        const int ft = args.dp_tiles + static_cast<int>(sk_start(cc, P, U) / args.num_k_blocks);
+        const int s = (ft == tile) ? 2 * cc : 2 * cc + 1;
+        return reinterpret_cast<const float4*>(args.partials + static_cast<size_t>(s) * kNPad * 128);
+      };
+      constexpr int kPass = kNPad < 64 ? kNPad : 64;  // columns per reduction pass
+      constexpr int kQ = kPass / 4;                    // float4 per thread per pass
+      auto store_row = [&](const float4 (&sum)[kQ], int c) {
+        if (n < args.N) {
+          const float* f = reinterpret_cast<const float*>(sum);
+#pragma unroll
+          for (int j = 0; j < kPass; ++j)
+            if (c + j < args.M)
+              args.d[static_cast<long long>(c + j) * args.ldd + n] = __float2bfloat16_rn(f[j]);
+        }
+      };
+      if (early_last) {
+        __threadfence();
+        const int nc = c1 - c0 + 1;
+#pragma unroll 1
+        for (int c = 0; c < kNPad; c += kPass) {
+          float4 sum[kQ];
+#pragma unroll
+          for (int q = 0; q < kQ; ++q) sum[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int i = 0; i < nc; ++i) {
+            float4 x[kQ];
+            if (c0 + i == static_cast<int>(blockIdx.x)) {
+#pragma unroll
+              for (int h = 0; h < kPass / 16; ++h) {
+                uint32_t v[16];
+                ptx::tmem_ld_32x32b_x16(acc + c + 16 * h, v);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  x[4 * h + q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                             __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+              }
+            } else {
+              const float4* sx = slot_of(c0 + i);
+#pragma unroll
+              for (int q = 0; q < kQ; ++q) x[q] = __ldcg(sx + (c / 4 + q) * 128 + tid);
+            }
+#pragma unroll
+            for (int q = 0; q < kQ; ++q) {
+              sum[q].x += x[q].x; sum[q].y += x[q].y; sum[q].z += x[q].z; sum[q].w += x[q].w;
+            }
+          }
+          store_row(sum, c);
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(acc_empty_bar(buf));
+        if (tid == 0) args.counters[tile] = 0u;
+        ptx::named_barrier(1, 128);
+        ++seg;
+        continue;
+      }
       float* part = nullptr;
       if (!whole) {
         const int s = (tile == first_tile) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
@@ -306,12 +383,9 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(acc_empty_bar(buf));
       if (!whole && kTiles == 1) {
-        // Publish the partial, count arrivals; the last contributor reduces.
+        // Publish the slot, count arrivals; the contributor that arrives last sums.
         __threadfence();
         ptx::named_barrier(1, 128);
-        const long long t_u0 = static_cast<long long>(tile - args.dp_tiles) * args.num_k_blocks;
-        const int c0 = static_cast<int>(sk_owner(t_u0, P, U));
-        const int c1 = static_cast<int>(sk_owner(t_u0 + args.num_k_blocks - 1, P, U));
         if (tid == 0) {
           const unsigned int prev = atomicAdd(&args.counters[tile], 1u);
           slot[1] = (prev == static_cast<unsigned int>(c1 - c0)) ? 1u : 0u;
@@ -319,16 +393,8 @@ __global__ void __launch_bounds__(192, 1)
         ptx::named_barrier(1, 128);
         if (slot[1] != 0u) {
           __threadfence();
-          // Sum the contributors' slots in contributor order (deterministic). The
-          // loop is latency-bound, so each pass covers up to 64 columns and keeps
-          // two contributors' loads (2 x 16 float4 per thread) in flight.
-          auto slot_of = [&](int cc) {
-            const int ft = args.dp_tiles + static_cast<int>(sk_start(cc, P, U) / args.num_k_blocks);
-            const int s = (ft == tile) ? 2 * cc : 2 * cc + 1;
-            return reinterpret_cast<const float4*>(args.partials + static_cast<size_t>(s) * kNPad * 128);
-          };
-          constexpr int kPass = kNPad < 64 ? kNPad : 64;  // columns per pass
-          constexpr int kQ = kPass / 4;                    // float4 per thread per pass
+          // Contributor order, two contributors' loads (2 x 16 float4 per thread)
+          // in flight per step: the loop is latency-bound.
           const int nc = c1 - c0 + 1;
 #pragma unroll 1
           for (int c = 0; c < kNPad; c += kPass) {
@@ -360,13 +426,7 @@ __global__ void __launch_bounds__(192, 1)
                 sum[q].x += x[q].x; sum[q].y += x[q].y; sum[q].z += x[q].z; sum[q].w += x[q].w;
               }
             }
-            if (n < args.N) {
-              const float* f = reinterpret_cast<const float*>(sum);
-#pragma unroll
-              for (int j = 0; j < kPass; ++j)
-                if (c + j < args.M)
-                  args.d[static_cast<long long>(c + j) * args.ldd + n] = __float2bfloat16_rn(f[j]);
-            }
+            store_row(sum, c);
           }
           if (tid == 0) args.counters[tile] = 0u;
         }

@@ -37,6 +37,8 @@ def test_struct_layouts_match_header():
     assert ctypes.sizeof(_lib.GemmConfigC) == 16 * 4
     assert ctypes.sizeof(_lib.GemmInfoC) == 14 * 4 + 8
     assert _lib.GemmInfoC.scheduler.offset == 13 * 4
+    assert ctypes.sizeof(_lib.EpilogueC) == 80
+    assert _lib.EpilogueC.out_dtype.offset == 32 and _lib.EpilogueC.d_scales.offset == 40
 
 
 def test_status_strings():
