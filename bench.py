@@ -9,10 +9,11 @@ D[:, r*N/g:(r+1)*N/g] from all of A and its slice of B), total work fixed.
 A step is one GEMM launch over resident inputs. Operands (256 MiB + 256 MiB
 E4M3 + scales at 1 GPU) exceed the 126 MB L2, so no L2 flush is done between
 steps. ``value`` = 2*M*N*K*steps / (max over ranks of the device time of the
-timed region). ``e2e`` repeats the measurement through the library's host-buffer
-entry (``cutex_mxfp8_gemm_host``) with pinned host buffers: each step copies A,
-B, SFA, SFB host->device, runs the GEMM in blocks and copies D device->host,
-copies and blocks overlapped, all inside the CUDA-event timed interval.
+timed region). ``e2e`` repeats the measurement from pinned host buffers, inside the
+CUDA-event timed interval: on 1 GPU through the library's host-buffer entry
+(``cutex_mxfp8_gemm_host``: A, B, SFA, SFB in, D out, copies and block GEMMs
+overlapped); on N GPUs through ``ShardedHostGemm`` (each rank copies 1/N of A and
+its B slice in, A is all-gathered over NVLink, D slices come back in row blocks).
 
 ``--impl reference`` times the contract's CPU path (dequantise, fp32 matmul,
 cast to BF16: the oracle port) on the host cores, on bounded row/column
@@ -431,22 +432,47 @@ def bench_cutex(args):
         achieved = flops_launch / (launch_avg_ms / 1e3) / 1e12
         peak, peak_src = fp8_peak(peaks, source, long_timed)
 
-    # ---- end to end through the C ABI with pinned host buffers
+    # ---- end to end through the library with pinned host buffers
     e2e = None
     if args.e2e_steps > 0:
-        ha = a.cpu().pin_memory()
         hb = b.cpu().pin_memory()
-        hsa = sfa.cpu().pin_memory()
         hsb = sfb.cpu().pin_memory()
         hd = torch.empty(d.shape, dtype=d.dtype).pin_memory()
-        from cutex_b200.kernels import HostGemm
+        if world == 1:
+            from cutex_b200.kernels import HostGemm
 
-        # The library's host-buffer entry: H2D copies, block GEMMs and D2H copies
-        # overlapped on its own streams, joined back into `stream`.
-        host_gemm = HostGemm(m, n_local, k, device=device, config=cfg, blocks=args.e2e_blocks)
+            # The library's host-buffer entry: H2D copies, block GEMMs and D2H
+            # copies overlapped on its own streams, joined back into `stream`.
+            ha = a.cpu().pin_memory()
+            hsa = sfa.cpu().pin_memory()
+            host_gemm = HostGemm(m, n_local, k, device=device, config=cfg, blocks=args.e2e_blocks)
 
-        def e2e_step():
-            host_gemm(ha, hb, hsa, hsb, hd, stream=stream)
+            def e2e_step():
+                host_gemm(ha, hb, hsa, hsb, hd, stream=stream)
+
+            h2d = ha.numel() + hb.numel() + hsa.numel() + hsb.numel()
+            d2h = hd.numel() * hd.element_size()
+            path = (f"cutex_mxfp8_gemm_host C ABI (HostGemm, {args.e2e_blocks}x{args.e2e_blocks} blocks), "
+                    "pinned host A/B/SFA/SFB in, D out")
+        else:
+            from cutex_b200.sharding import ShardedHostGemm
+
+            # Each rank copies 1/world of A (A is the same on every rank) plus its
+            # B slice in, NCCL gathers A over NVLink, D[:, n0:n1] comes back in row
+            # blocks while the next block computes.
+            host_gemm = ShardedHostGemm(m, n, k, config=cfg, device=device)
+            r0, r1 = host_gemm.rows.n0, host_gemm.rows.n1
+            sf_row = k // 32
+            ha = a[r0:r1].cpu().pin_memory()
+            hsa = sfa[r0 * sf_row:r1 * sf_row].cpu().pin_memory()
+
+            def e2e_step():
+                host_gemm(ha, hsa, hb, hsb, hd, stream=stream)
+
+            h_in, h_out = host_gemm.host_bytes()
+            h2d, d2h = h_in * world, h_out * world
+            path = ("ShardedHostGemm: pinned host rows of A (1/world per rank) + B slice in, "
+                    "NCCL all-gather of A, D slice out in row blocks")
 
         with torch.cuda.stream(stream):
             e2e_step()
@@ -463,16 +489,13 @@ def bench_cutex(args):
         te = torch.tensor([s2.elapsed_time(e2)], dtype=torch.float64, device=device)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        h2d = (ha.numel() + hb.numel() + hsa.numel() + hsb.numel()) * world
-        d2h = hd.numel() * hd.element_size() * world
         e2e = {
             "value": total_flops * args.e2e_steps / (float(te[0]) / 1e3) / 1e12,
             "unit": "TFLOP/s",
             "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
             "steps": args.e2e_steps,
-            "path": f"cutex_mxfp8_gemm_host C ABI (HostGemm, {args.e2e_blocks}x{args.e2e_blocks} blocks), "
-                    "pinned host A/B/SFA/SFB in, D out",
+            "path": path,
         }
         del host_gemm, ha, hb, hsa, hsb, hd
 

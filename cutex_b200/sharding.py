@@ -142,4 +142,89 @@ class FusedAllGatherGemm:
         self._mappings = []
 
 
-__all__ = ["SHARD_ALIGN", "FusedAllGatherGemm", "Shard", "allgather_columns", "scale_rows_slice", "shard_bounds"]
+class ShardedHostGemm:
+    """N-sharded GEMM from pinned host buffers, with A's host-to-device copy split across the ranks.
+
+    Every rank needs all of A, but A is the same on every rank: each rank copies
+    only its ``rows`` (M / world rows of A and their scale rows) over its own host
+    link, and one NCCL all-gather over NVLink assembles A on every GPU. Each rank
+    copies its B slice in on a second stream meanwhile, runs the GEMM of its
+    D[:, n0:n1] in row blocks and copies each finished block back to the host
+    while the next one computes. Host link traffic per rank: 1/world of A plus its
+    own B slice and D slice. M must be a multiple of 128 * world.
+    """
+
+    def __init__(self, m: int, n: int, k: int, group=None, config=None, device=None, blocks: int = 4):
+        import torch
+        import torch.distributed as dist
+
+        from .kernels.dense_gemm import GemmConfig
+        from .kernels.dense_gemm_contract import scale_buffer_bytes
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if m % (128 * self.world):
+            raise ValueError(f"M={m} must be a multiple of 128 * world = {128 * self.world}")
+        self.cols = shard_bounds(n, self.world, self.rank)
+        self.rows = shard_bounds(m, self.world, self.rank, align=128)
+        self.m, self.n, self.k = m, n, k
+        self.config = config or GemmConfig()
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        u8 = torch.uint8
+        n_loc, m_loc = self.cols.n, self.rows.n
+        self.sf_row = k // 32
+        self.a = torch.empty(m * k, dtype=u8, device=dev)
+        self.sfa = torch.empty(scale_buffer_bytes(m, k), dtype=u8, device=dev)
+        self.a_part = torch.empty(m_loc * k, dtype=u8, device=dev)
+        self.sfa_part = torch.empty(m_loc * self.sf_row, dtype=u8, device=dev)
+        self.b = torch.empty(n_loc, k, dtype=u8, device=dev)
+        self.sfb = torch.empty(scale_buffer_bytes(n_loc, k), dtype=u8, device=dev)
+        self.d = torch.empty(m, n_loc, dtype=torch.bfloat16, device=dev)
+        blk = -(-m // blocks)
+        blk = -(-blk // 256) * 256
+        self.row_blocks = [(r0, min(m, r0 + blk)) for r0 in range(0, m, blk)]
+        self._b_stream = torch.cuda.Stream(dev)
+        self._d_stream = torch.cuda.Stream(dev)
+
+    def host_bytes(self) -> tuple[int, int]:
+        """(host-to-device, device-to-host) bytes this rank moves per call."""
+
+        h2d = self.a_part.numel() + self.sfa_part.numel() + self.b.numel() + self.sfb.numel()
+        return h2d, self.d.numel() * 2
+
+    def __call__(self, a_rows_host, sfa_rows_host, b_host, sfb_host, d_host, stream=None):
+        """a_rows_host: this rank's ``rows`` of A [m_loc, K] and sfa_rows_host their scale rows
+        (whole 128-row blocks of the swizzled buffer); b_host / sfb_host: this rank's B slice and
+        its scales; d_host [M, n_loc]: D[:, n0:n1]. Pinned host tensors. Asynchronous on ``stream``."""
+
+        import torch
+        import torch.distributed as dist
+
+        from .kernels.dense_gemm import dense_gemm
+
+        s = torch.cuda.current_stream() if stream is None else stream
+        self._b_stream.wait_stream(s)
+        with torch.cuda.stream(self._b_stream):
+            self.b.copy_(b_host, non_blocking=True)
+            self.sfb.copy_(sfb_host.reshape(-1), non_blocking=True)
+        with torch.cuda.stream(s):
+            self.a_part.copy_(a_rows_host.reshape(-1), non_blocking=True)
+            self.sfa_part.copy_(sfa_rows_host.reshape(-1), non_blocking=True)
+            dist.all_gather_into_tensor(self.a, self.a_part, group=self.group)
+            dist.all_gather_into_tensor(self.sfa[: self.m * self.sf_row], self.sfa_part, group=self.group)
+            s.wait_stream(self._b_stream)
+            a2 = self.a.view(self.m, self.k)
+            for r0, r1 in self.row_blocks:
+                dense_gemm(a2[r0:r1], self.b, self.sfa[r0 * self.sf_row:], self.sfb, self.d[r0:r1], stream=s,
+                           config=self.config)
+                ev = torch.cuda.Event()
+                ev.record(s)
+                self._d_stream.wait_event(ev)
+                with torch.cuda.stream(self._d_stream):
+                    d_host[r0:r1].copy_(self.d[r0:r1], non_blocking=True)
+            s.wait_stream(self._d_stream)
+
+
+__all__ = ["SHARD_ALIGN", "FusedAllGatherGemm", "Shard", "ShardedHostGemm", "allgather_columns",
+           "scale_rows_slice", "shard_bounds"]
