@@ -675,23 +675,39 @@ extern "C" int cutex_ipc_close(void* mapping) {
   return cudaIpcCloseMemHandle(mapping) == cudaSuccess ? CUTEX_OK : CUTEX_ERR_CUDA;
 }
 
-extern "C" int cutex_mxfp8_gemm_allgather(const void* a, const void* b, const void* sfa, const void* sfb, void* d,
-                                          int64_t M, int64_t N, int64_t K, int64_t ldd, const void* const* peer_d,
-                                          int32_t num_peers, void* map_buffer, int64_t map_buffer_bytes,
-                                          const cutex_gemm_config* cfg, cutex_stream_t stream) {
-  if (a == nullptr || b == nullptr || sfa == nullptr || sfb == nullptr || d == nullptr || peer_d == nullptr ||
-      map_buffer == nullptr)
-    return CUTEX_ERR_INVALID_ARGUMENT;
+extern "C" int cutex_mxfp8_allgather_maps(const void* const* peer_d, int32_t num_peers, int64_t M, int64_t N,
+                                          int64_t ldd, void* map_buffer, int64_t map_buffer_bytes,
+                                          cutex_stream_t stream) {
+  if (peer_d == nullptr || map_buffer == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
   if (num_peers < 1 || num_peers > kMaxGatherPeers) return CUTEX_ERR_INVALID_ARGUMENT;
   if (map_buffer_bytes < static_cast<int64_t>(num_peers) * static_cast<int64_t>(sizeof(CUtensorMap)))
     return CUTEX_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(map_buffer) & 63u) != 0) return CUTEX_ERR_ALIGN;  // CUtensorMap alignment
+  if (M < 1 || N < 1 || M > kMaxDim || N > kMaxDim) return CUTEX_ERR_SHAPE;
+  if (N % 16 != 0 || ldd < N || ldd % 8 != 0 || ldd > kMaxDim) return CUTEX_ERR_ALIGN;
+  for (int p = 0; p < num_peers; ++p)
+    if (peer_d[p] == nullptr || !aligned16(peer_d[p])) return CUTEX_ERR_ALIGN;
+  CUtensorMap maps[kMaxGatherPeers];
+  for (int p = 0; p < num_peers; ++p)
+    if (!encode_output(&maps[p], const_cast<void*>(peer_d[p]), M, N, ldd)) return CUTEX_ERR_CUDA;
+  // From host memory: the call returns once the array has been staged.
+  return cudaMemcpyAsync(map_buffer, maps, sizeof(CUtensorMap) * num_peers, cudaMemcpyHostToDevice,
+                         reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? CUTEX_OK
+             : CUTEX_ERR_CUDA;
+}
+
+extern "C" int cutex_mxfp8_gemm_allgather(const void* a, const void* b, const void* sfa, const void* sfb, void* d,
+                                          int64_t M, int64_t N, int64_t K, int64_t ldd, const void* map_buffer,
+                                          int32_t num_peers, const cutex_gemm_config* cfg, cutex_stream_t stream) {
+  if (a == nullptr || b == nullptr || sfa == nullptr || sfb == nullptr || d == nullptr || map_buffer == nullptr)
+    return CUTEX_ERR_INVALID_ARGUMENT;
+  if (num_peers < 1 || num_peers > kMaxGatherPeers) return CUTEX_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(map_buffer) & 63u) != 0) return CUTEX_ERR_ALIGN;
   int st = validate_shape(M, N, K);
   if (st != CUTEX_OK) return st;
   if (ldd < N || ldd % 8 != 0 || ldd > kMaxDim) return CUTEX_ERR_ALIGN;
   if (!aligned16(a) || !aligned16(b) || !aligned16(sfa) || !aligned16(sfb) || !aligned16(d)) return CUTEX_ERR_ALIGN;
-  for (int p = 0; p < num_peers; ++p)
-    if (peer_d[p] == nullptr || !aligned16(peer_d[p])) return CUTEX_ERR_ALIGN;
   DeviceState* ds = nullptr;
   st = current_device_state(&ds);
   if (st != CUTEX_OK) return st;
@@ -702,18 +718,10 @@ extern "C" int cutex_mxfp8_gemm_allgather(const void* a, const void* b, const vo
   st = resolve_plan(&c2, M, N, K, ds->sm_count, &plan);
   if (st != CUTEX_OK) return st;
   if (plan.variant == nullptr || plan.variant->fn_epi[3] == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
-  // The peers' D regions as TMA store descriptors, placed in map_buffer in
-  // stream order (the copy stages the host array before returning).
-  CUtensorMap maps[kMaxGatherPeers];
-  for (int p = 0; p < num_peers; ++p)
-    if (!encode_output(&maps[p], const_cast<void*>(peer_d[p]), M, N, ldd)) return CUTEX_ERR_CUDA;
-  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemcpyAsync(map_buffer, maps, sizeof(CUtensorMap) * num_peers, cudaMemcpyHostToDevice, s) != cudaSuccess)
-    return CUTEX_ERR_CUDA;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
-  return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd, s, nullptr, 0, nullptr,
-                     static_cast<const CUtensorMap*>(map_buffer), num_peers);
+  return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd, reinterpret_cast<cudaStream_t>(stream), nullptr, 0,
+                     nullptr, static_cast<const CUtensorMap*>(map_buffer), num_peers);
 }
 
 extern "C" int cutex_mxfp8_gemm_trace(const void* a, const void* b, const void* sfa,

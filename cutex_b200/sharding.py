@@ -109,6 +109,12 @@ class FusedAllGatherGemm:
             peers.append(ptr.value + self.shard.n0 * 2)  # this rank's columns in peer r's copy
         self._peers = (ctypes.c_void_p * len(peers))(*peers)
         self._maps = torch.empty(128 * len(peers), dtype=torch.uint8, device=dev)
+        # The peers' TMA store descriptors, written once (a host copy that waits
+        # for the stream would otherwise serialise every call).
+        _lib.check(lib.cutex_mxfp8_allgather_maps(self._peers, len(peers), m, self.shard.n, n, self._maps.data_ptr(),
+                                                  self._maps.numel(), torch.cuda.current_stream().cuda_stream),
+                   "cutex_mxfp8_allgather_maps")
+        torch.cuda.current_stream().synchronize()  # descriptors in place before any stream's GEMM reads them
         self._cfg = (config or GemmConfig()).to_c()
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
 
@@ -124,8 +130,8 @@ class FusedAllGatherGemm:
         handle = _stream_handle(stream)
         status = _lib.load().cutex_mxfp8_gemm_allgather(
             a.data_ptr(), b_local.data_ptr(), sfa.data_ptr(), sfb_local.data_ptr(),
-            self.d_full.data_ptr() + self.shard.n0 * 2, self.m, self.shard.n, self.k, self.n, self._peers,
-            len(self._peers), self._maps.data_ptr(), self._maps.numel(), ctypes.byref(self._cfg), handle)
+            self.d_full.data_ptr() + self.shard.n0 * 2, self.m, self.shard.n, self.k, self.n, self._maps.data_ptr(),
+            len(self._peers), ctypes.byref(self._cfg), handle)
         _lib.check(status, "cutex_mxfp8_gemm_allgather")
         # Cross-rank barrier in stream order: every rank's pushes have landed.
         s = stream if stream is not None and not isinstance(stream, int) else torch.cuda.current_stream()

@@ -168,25 +168,34 @@ CUTEX_API int cutex_ipc_import(const void* handle, int64_t offset, void** dev_pt
 CUTEX_API int cutex_ipc_close(void* mapping);
 
 /*
+ * TMA store descriptors of the peers' copies of D for cutex_mxfp8_gemm_allgather:
+ * peer_d[p] = the first element of this rank's region [M, N] (row stride ldd)
+ * inside peer p's full D, mapped with cutex_ipc_import (16-byte aligned;
+ * num_peers <= 7). Written into map_buffer (device memory, >= 128 * num_peers
+ * bytes, 64-byte aligned) on `stream` by a copy from host memory, which waits
+ * for the stream: call it once, when the peers are mapped, not per GEMM. The
+ * peer stores of later GEMMs stay inside the regions described here.
+ */
+CUTEX_API int cutex_mxfp8_allgather_maps(const void* const* peer_d, int32_t num_peers, int64_t M, int64_t N,
+                                         int64_t ldd, void* map_buffer, int64_t map_buffer_bytes,
+                                         cutex_stream_t stream);
+
+/*
  * N-sharded GEMM with the all-gather of D fused into the epilogue: computes
  * this rank's D[:, n0:n0+N] (d points at its first element inside this
  * rank's full D, row stride ldd) and stores every finished 32 x 64 chunk, by
- * TMA from the same shared-memory staging buffer, also into each peer's full
- * D (peer_d[p] = the same element in peer p's copy, mapped with
- * cutex_ipc_import; 16-byte aligned; num_peers <= 7), so the gather overlaps
- * the GEMM tile by tile over NVLink. map_buffer: device memory for the peers'
- * TMA descriptors, >= 128 * num_peers bytes, 64-byte aligned, written on
- * `stream` before the launch (not capturable into a CUDA graph). The peers'
- * copies are complete when every rank's call has completed: order readers
- * after a cross-rank barrier on the stream (e.g. a one-element NCCL
+ * TMA from the same shared-memory staging buffer, also into each peer's copy
+ * through the num_peers descriptors that cutex_mxfp8_allgather_maps placed in
+ * map_buffer, so the gather overlaps the GEMM tile by tile over NVLink. The
+ * peers' copies are complete when every rank's call has completed: order
+ * readers after a cross-rank barrier on the stream (e.g. a one-element NCCL
  * all-reduce). Kernel choice as cutex_mxfp8_gemm_ex (no skinny kernel).
  * Replaces the GEMM + ncclAllGather + re-layout sequence (one NCCL
  * collective after the kernel, then a permute).
  */
 CUTEX_API int cutex_mxfp8_gemm_allgather(const void* a, const void* b, const void* sfa, const void* sfb, void* d,
-                                         int64_t M, int64_t N, int64_t K, int64_t ldd, const void* const* peer_d,
-                                         int32_t num_peers, void* map_buffer, int64_t map_buffer_bytes,
-                                         const cutex_gemm_config* cfg, cutex_stream_t stream);
+                                         int64_t M, int64_t N, int64_t K, int64_t ldd, const void* map_buffer,
+                                         int32_t num_peers, const cutex_gemm_config* cfg, cutex_stream_t stream);
 
 /*
  * Resolve a configuration for a shape without launching anything.

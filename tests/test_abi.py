@@ -175,3 +175,31 @@ def test_fused_epilogue_argument_checks_without_launching():
     e = _lib.EpilogueC(alpha=1.0)
     e.reserved[2] = 1
     assert call(e) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+
+
+def test_allgather_argument_checks_without_launching():
+    lib = _lib.load()
+    p = 256  # 16-byte aligned placeholder: every case below is rejected before any CUDA call
+    peers = (ctypes.c_void_p * 2)(p, p)
+
+    def maps(n_peers=2, M=256, N=256, ldd=512, buf=p, nbytes=256):
+        return lib.cutex_mxfp8_allgather_maps(peers, n_peers, M, N, ldd, buf, nbytes, None)
+
+    assert maps(n_peers=0) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    assert maps(n_peers=8) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    assert maps(nbytes=128) == _lib.CUTEX_ERR_WORKSPACE  # 128 bytes per descriptor
+    assert maps(buf=p + 16) == _lib.CUTEX_ERR_ALIGN
+    assert maps(ldd=128) == _lib.CUTEX_ERR_ALIGN
+    assert maps(M=0) == _lib.CUTEX_ERR_SHAPE
+    assert lib.cutex_mxfp8_allgather_maps((ctypes.c_void_p * 2)(p, p + 2), 2, 256, 256, 512, p, 256, None) == (
+        _lib.CUTEX_ERR_ALIGN)
+
+    cfg = _lib.make_config()
+
+    def gemm(n_peers=2, M=256, N=256, K=128, ldd=512, buf=p):
+        return lib.cutex_mxfp8_gemm_allgather(p, p, p, p, p, M, N, K, ldd, buf, n_peers, ctypes.byref(cfg), None)
+
+    assert gemm(n_peers=0) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    assert gemm(buf=None) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    assert gemm(buf=p + 32) == _lib.CUTEX_ERR_ALIGN
+    assert gemm(ldd=200) == _lib.CUTEX_ERR_ALIGN
