@@ -117,6 +117,16 @@ bool encode_output(CUtensorMap* map, void* p, int64_t M, int64_t N, int64_t ldd)
                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
 }
 
+// bf16 output [M, N] of the skinny kernel: 32 x 32 boxes (one epilogue warp's
+// 32 columns), no swizzle.
+bool encode_output_skinny(CUtensorMap* map, void* p, int64_t M, int64_t N, int64_t ldd) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ldd) * 2u};
+  const uint32_t box[2] = {32u, 32u};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_NONE);
+}
+
 // e4m3 output [M, N] with row stride ldd bytes, 32 x 64 boxes, 64-byte swizzle.
 bool encode_output_fp8(CUtensorMap* map, void* p, int64_t M, int64_t N, int64_t ldd) {
   const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
@@ -300,14 +310,13 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
     int grid = sm_count;
     if (cfg.max_ctas != 0) grid = std::min(grid, cfg.max_ctas);
     const int64_t tiles128 = (N + 127) / 128;
-    // Split-K pays off while the fp32 partial slots stay small (padded M <= 32);
-    // for wider M the AUTO choice keeps whole tiles (measured: M = 128, N = 28672,
-    // K = 8192 streams at 0.77 of HBM with whole 128-row tiles vs 0.64 split).
-    const bool auto_whole = cfg.kernel == CUTEX_KERNEL_AUTO && cfg.split_k == 0 && sv1->npad > 32;
+    // AUTO is stream-K for every padded M: each SM streams the same share of B,
+    // where whole tiles leave a second wave on 76 of 148 SMs (N = 28672).
+    // Measured at N = 28672, K = 8192: M = 128 44.7 us vs 46.9 us whole,
+    // M = 64 39.4 vs 41.8, M = 16 39.9 vs 40.5.
     // Two 128-row B tiles per CTA tile (tile_n 256, whole tiles only): one A
-    // stage serves both tiles. Explicit only: measured at M = 64 / 128,
-    // N = 28672, K = 8192 it streams 3-5 % slower than single tiles (one wave of
-    // 112 CTAs at the same per-SM rate instead of 148 + 76).
+    // stage serves both tiles. Explicit only: measured at M = 64 / 128 it
+    // streams slower than single tiles (one wave of 112 CTAs).
     const int tiles = cfg.tile_n == 256 ? 2 : 1;
     SkinnyVariant* sv = find_skinny(M, tiles);
     if (sv == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;  // no double-tile build for this padded M
@@ -322,7 +331,7 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
     plan->raster_group = 1;
     plan->raster_along_n = 0;
     const int64_t units = static_cast<int64_t>(plan->num_n_tiles) * (K / 128);
-    plan->streamk = (cfg.split_k == 1 || auto_whole || tiles == 2) ? 0 : 1;
+    plan->streamk = (cfg.split_k == 1 || tiles == 2) ? 0 : 1;
     grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, plan->streamk ? units : plan->num_n_tiles)));
     plan->grid_ctas = grid;
     plan->dp_tiles = 0;
@@ -457,10 +466,11 @@ int launch_skinny(const Plan& plan, int dev, const void* a, const void* b, const
                   const void* sfb, void* d, int64_t M, int64_t N, int64_t K, int64_t ldd,
                   void* workspace, cudaStream_t stream) {
   SkinnyVariant* v = plan.skinny;
-  CUtensorMap tb, ta, tsb, tsa;
+  CUtensorMap tb, ta, tsb, tsa, td;
   if (!encode_operand(&tb, b, N, K, static_cast<uint32_t>(128 * v->tiles)) ||
       !encode_operand(&ta, a, M, K, static_cast<uint32_t>(v->npad)) ||
-      !encode_scales(&tsb, sfb, N, K, static_cast<uint32_t>(v->tiles)) || !encode_scales(&tsa, sfa, M, K, 1))
+      !encode_scales(&tsb, sfb, N, K, static_cast<uint32_t>(v->tiles)) || !encode_scales(&tsa, sfa, M, K, 1) ||
+      !encode_output_skinny(&td, d, M, N, ldd))
     return CUTEX_ERR_CUDA;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
@@ -490,7 +500,15 @@ int launch_skinny(const Plan& plan, int dev, const void* a, const void* b, const
   lc.blockDim = dim3(192, 1, 1);
   lc.dynamicSmemBytes = static_cast<size_t>(v->smem_bytes);
   lc.stream = stream;
-  void* params[] = {&tb, &ta, &tsb, &tsa, &args};
+  // Programmatic dependent launch: the kernel waits (griddepcontrol.wait) for
+  // the previous kernel of the stream before touching global memory, so its
+  // launch and set-up overlap that kernel's last CTAs.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  void* params[] = {&tb, &ta, &tsb, &tsa, &td, &args};
   if (cudaLaunchKernelExC(&lc, v->fn, params) != cudaSuccess) return CUTEX_ERR_CUDA;
   return CUTEX_OK;
 }

@@ -58,7 +58,11 @@ struct SkinnyCfg {
   static constexpr int kOffA = kOffB + kStages * kBBytes;
   static constexpr int kOffSFB = kOffA + kStages * kABytes;  // B's scale chunks (MMA A side)
   static constexpr int kOffSFA = kOffSFB + kStages * kSFBBytes;  // A's scale chunk (MMA B side)
-  static constexpr int kOffBar = align_up(kOffSFA + kStages * 512, 8);
+  // D staging: per epilogue warp kEpiBufs boxes of [32 rows m][32 columns n] bf16.
+  static constexpr int kEpiBufs = kNPad > 32 ? 2 : 1;
+  static constexpr int kDBoxBytes = 32 * 32 * 2;
+  static constexpr int kOffD = kOffSFA + kStages * 512;
+  static constexpr int kOffBar = align_up(kOffD + 4 * kEpiBufs * kDBoxBytes, 8);
   static constexpr int kNumBars = 2 * kStages + 4;
   static constexpr int kOffSlot = kOffBar + kNumBars * 8;  // TMEM address + last-arrival flag
   static constexpr int kSmemBytes = kOffSlot + 16 + 1024;
@@ -76,6 +80,28 @@ struct SkinnyCfg {
   static_assert(kSFCol + 2 * kSFBufCols <= kTmemCols, "TMEM plan");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
 };
+
+// Converts kCnt values of this thread's D column n (rows m0 .. m0 + kCnt - 1) to
+// bf16 in the warp's next [32 m][32 n] staging box, then lane 0 stores the box
+// at (n0 of the warp, m0) with TMA; rows and columns outside D are clipped by
+// the tensor map. The box is reused once its previous store has read it.
+template <int kCnt, int kEpiBufs>
+__device__ __forceinline__ void skinny_emit(const float (&v)[kCnt], __nv_bfloat16* stage, uint32_t stage_addr,
+                                            int& buf, uint32_t lane, const CUtensorMap* tmap_d, int n0, int m0) {
+  static_assert(kCnt == 16 || kCnt == 32, "rows per box");
+  if (lane == 0) ptx::bulk_wait_group_read<kEpiBufs - 1>();
+  __syncwarp();
+  __nv_bfloat16* box = stage + buf * 32 * 32;
+#pragma unroll
+  for (int j = 0; j < kCnt; ++j) box[j * 32 + lane] = __float2bfloat16_rn(v[j]);
+  ptx::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    ptx::tma_store_2d(tmap_d, stage_addr + static_cast<uint32_t>(buf) * 2048u, n0, m0);
+    ptx::bulk_commit_group();
+  }
+  buf = (buf + 1) % kEpiBufs;
+}
 
 // Units [start(c), start(c+1)) of CTA c.
 __device__ __forceinline__ long long sk_start(long long c, long long P, long long U) {
@@ -129,7 +155,8 @@ __global__ void __launch_bounds__(192, 1)
     mxfp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_a,
                         const __grid_constant__ CUtensorMap tmap_sfb,
-                        const __grid_constant__ CUtensorMap tmap_sfa, const SkinnyArgs args) {
+                        const __grid_constant__ CUtensorMap tmap_sfa,
+                        const __grid_constant__ CUtensorMap tmap_d, const SkinnyArgs args) {
   using C = SkinnyCfg<kNPad, kStages, kTiles>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = ptx::smem_u32(smem_raw);
@@ -169,6 +196,12 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = slot[0];
+  // Launched with programmatic stream serialization: the set-up above may
+  // overlap the end of the previous kernel in the stream; no global memory is
+  // touched before that kernel has completed. The next launch of this kernel
+  // may be scheduled from here on (its CTAs take SMs as these CTAs exit).
+  ptx::grid_dependency_wait();
+  ptx::launch_dependents();
 
   SegmentWalker walk;
   walk.init(args);
@@ -259,6 +292,9 @@ __global__ void __launch_bounds__(192, 1)
     const int first_tile =
         args.streamk ? args.dp_tiles + static_cast<int>(sk_start(blockIdx.x, P, U) / args.num_k_blocks) : -1;
     const uint32_t tid = threadIdx.x;  // 0..127: row of the B tile = column of D
+    const uint32_t dstage_addr = smem + C::kOffD + static_cast<uint32_t>(warp) * C::kEpiBufs * C::kDBoxBytes;
+    __nv_bfloat16* dstage = reinterpret_cast<__nv_bfloat16*>(smem_ptr + C::kOffD + warp * C::kEpiBufs * C::kDBoxBytes);
+    int dbuf = 0;
     int seg = 0;
     while (walk.next(args, tile, kb0, kb1)) {
       const int buf = seg % C::kAccBufs, use = seg / C::kAccBufs;
@@ -269,6 +305,7 @@ __global__ void __launch_bounds__(192, 1)
       const bool whole = kb0 == 0 && kb1 == args.num_k_blocks;
       if (!whole && kTiles != 1) atomicCAS(status, 0, kDevBadTile);  // the host never splits double tiles
       const int n = tile * kTiles * 128 + static_cast<int>(tid);
+      const int n0w = tile * kTiles * 128 + warp * 32;  // first D column of this warp's boxes
       // A tile cut between CTAs: the contributors of its K-range and whether all
       // the others have already published their slots. If so this CTA is the
       // last: it sums their slots with its own accumulator read straight from
@@ -297,12 +334,24 @@ __global__ void __launch_bounds__(192, 1)
       constexpr int kPass = kNPad < 64 ? kNPad : 64;  // columns per reduction pass
       constexpr int kQ = kPass / 4;                    // float4 per thread per pass
       auto store_row = [&](const float4 (&sum)[kQ], int c) {
-        if (n < args.N) {
-          const float* f = reinterpret_cast<const float*>(sum);
+        if constexpr (kPass == 16) {
+          float f[16];
 #pragma unroll
-          for (int j = 0; j < kPass; ++j)
-            if (c + j < args.M)
-              args.d[static_cast<long long>(c + j) * args.ldd + n] = __float2bfloat16_rn(f[j]);
+          for (int q = 0; q < 4; ++q) {
+            f[4 * q] = sum[q].x; f[4 * q + 1] = sum[q].y; f[4 * q + 2] = sum[q].z; f[4 * q + 3] = sum[q].w;
+          }
+          skinny_emit<16, C::kEpiBufs>(f, dstage, dstage_addr, dbuf, lane, &tmap_d, n0w, c);
+        } else {
+#pragma unroll
+          for (int h = 0; h < kPass / 32; ++h) {
+            float f[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 x = sum[8 * h + q];
+              f[4 * q] = x.x; f[4 * q + 1] = x.y; f[4 * q + 2] = x.z; f[4 * q + 3] = x.w;
+            }
+            skinny_emit<32, C::kEpiBufs>(f, dstage, dstage_addr, dbuf, lane, &tmap_d, n0w, c + 32 * h);
+          }
         }
       };
       if (early_last) {
@@ -353,21 +402,35 @@ __global__ void __launch_bounds__(192, 1)
       }
 #pragma unroll 1
       for (int t = 0; t < kTiles; ++t) {
-        const int nt = n + t * 128;
+        if (whole) {
+          if constexpr (kNPad == 16) {
+            uint32_t v[16];
+            ptx::tmem_ld_32x32b_x16(acc + t * kNPad, v);
+            ptx::tmem_wait_ld();
+            float f[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(v[j]);
+            skinny_emit<16, C::kEpiBufs>(f, dstage, dstage_addr, dbuf, lane, &tmap_d, n0w + t * 128, 0);
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < kNPad; c += 32) {
+              uint32_t v[32];
+              ptx::tmem_ld_32x32b_x32(acc + t * kNPad + c, v);
+              ptx::tmem_wait_ld();
+              float f[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+              skinny_emit<32, C::kEpiBufs>(f, dstage, dstage_addr, dbuf, lane, &tmap_d, n0w + t * 128, c);
+            }
+          }
+          continue;
+        }
 #pragma unroll 1
         for (int c = 0; c < kNPad; c += 16) {
           uint32_t v[16];
           ptx::tmem_ld_32x32b_x16(acc + t * kNPad + c, v);
           ptx::tmem_wait_ld();
-          if (whole) {
-            if (nt < args.N) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                if (c + j < args.M)
-                  args.d[static_cast<long long>(c + j) * args.ldd + nt] = __float2bfloat16_rn(__uint_as_float(v[j]));
-              }
-            }
-          } else if (kTiles == 1) {
+          if (kTiles == 1) {
             // Slot layout [kNPad / 4][128 rows][4 columns]: one 16-byte store per
             // thread and column group, 512 contiguous bytes per warp.
             float4* part4 = reinterpret_cast<float4*>(part);
@@ -434,6 +497,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       ++seg;
     }
+    if (lane == 0) ptx::bulk_wait_group_all();  // D stores complete before the CTA exits
   }
 
   ptx::tc_fence_before();

@@ -54,6 +54,13 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
   return r;
 }
 
+// Programmatic dependent launch. wait: block until the grids this grid depends
+// on (the previous kernel of the stream, when launched with programmatic stream
+// serialization) have completed and their memory is visible. launch_dependents:
+// allow the next such grid to be scheduled (its CTAs still run their own wait).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");

@@ -67,9 +67,9 @@ typedef struct cutex_gemm_config {
   int32_t stages;         /* shared-memory ring depth */
   int32_t raster_group;   /* output tiles per rasterisation group (>= 1) */
   int32_t raster_along_n; /* 0: walk M inside a group, 1: walk N inside a group */
-  int32_t split_k;        /* skinny kernel: 0 = stream-K over all SMs (kernel AUTO: whole
-                             tiles when the padded M > 32), 1 = whole tiles, 2 = stream-K over
-                             all SMs, 3 = whole tiles for the full waves + stream-K remainder */
+  int32_t split_k;        /* skinny kernel: 0 = stream-K over all SMs, 1 = whole tiles,
+                             2 = stream-K over all SMs, 3 = whole tiles for the full waves +
+                             stream-K remainder */
   int32_t max_ctas;       /* cap on persistent CTAs (0 = one per SM) */
   int32_t epi_buffers;    /* epilogue staging buffers per warp (1 or 2) */
   int32_t sf_buffers;     /* rotating scale-factor TMEM buffers (1, 2 or 4) */

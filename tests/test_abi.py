@@ -120,7 +120,7 @@ def test_python_wrapper_rejects_with_value_errors():
     assert q["kernel"] == _lib.KERNEL_SKINNY and q["tile_m"] == 16 and q["split_k"] == 0
     assert q["workspace_bytes"] == 2 * 148 * 128 * 128 * 4 + 1024  # CPU-side default of 148 SMs
     q128 = query(128, 28672, 8192)
-    assert q128["tile_m"] == 128 and q128["split_k"] == 1 and q128["workspace_bytes"] == 0
+    assert q128["tile_m"] == 128 and q128["split_k"] == 0 and q128["workspace_bytes"] == q["workspace_bytes"]
     assert query(128, 28672, 8192, GemmConfig(kernel=_lib.KERNEL_SKINNY))["split_k"] == 0
     assert query(100, 256, 256, GemmConfig(split_k=1))["workspace_bytes"] == 0
     assert query(129, 256, 256)["kernel"] != _lib.KERNEL_SKINNY
