@@ -432,7 +432,7 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
   lc.blockDim = dim3(v->dynamic ? 224 : 192, 1, 1);
   lc.dynamicSmemBytes = static_cast<size_t>(v->smem_bytes);
   lc.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   if (cg == 2) {
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -457,6 +457,12 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
     if (!v->dynamic && plan.grid_ctas > 2 * max_clusters)
       lc.gridDim.x = static_cast<unsigned>(2 * max_clusters);
   }
+  // Programmatic dependent launch (the kernel waits with griddepcontrol.wait
+  // before its first global access).
+  attr[lc.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[lc.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs += 1;
   void* params[] = {&ta, &tb, &tsa, &tsb, &td, &args};
   if (cudaLaunchKernelExC(&lc, fn, params) != cudaSuccess) return CUTEX_ERR_CUDA;
   return CUTEX_OK;

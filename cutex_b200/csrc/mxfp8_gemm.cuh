@@ -448,6 +448,12 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
   if constexpr (kPair) ptx::cluster_sync(); else __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialization: the set-up above may
+  // overlap the end of the previous kernel in the stream; no global memory is
+  // touched before that kernel has completed. The next launch may be
+  // scheduled from here on (its CTAs take SMs as these CTAs exit).
+  ptx::grid_dependency_wait();
+  ptx::launch_dependents();
   Tracer<kTrace> tr;
   if (threadIdx.x == 0) trace_cta_time<kTrace>(args, 0);
   TileSource<kDynamic, kPair> src;
