@@ -61,6 +61,9 @@ def parse_args():
     p.add_argument("--no-graph", action="store_true", help="plain launches instead of one CUDA graph")
     p.add_argument("--sustained-s", type=float, default=2.0,
                    help="also run the launches back to back for this many seconds (0: skip)")
+    p.add_argument("--vs-cublaslt", type=int, default=0, metavar="ROUNDS",
+                   help="N = 1: also time cuBLASLt MXFP8 (torch._scaled_mm) on the same operands, alternating "
+                        "ROUNDS graph replays of each with this kernel's, and compare the outputs bitwise")
     p.add_argument("--measure-fp8-peak", action="store_true",
                    help="measure cuBLASLt MXFP8 (torch._scaled_mm) 8192^3: best-of-10 burst and 4 s sustained")
     p.add_argument("--dist", choices=("square", "llm"), default="square",
@@ -545,6 +548,11 @@ def bench_cutex(args):
         fused.close()
         del fused
 
+    # ---- the vendor library on the same operands (comparator only, never the product path)
+    cublaslt = None
+    if args.vs_cublaslt > 0 and world == 1:
+        cublaslt = compare_cublaslt(args, a, sfa, b, sfb, d, graph, step, stream, m, n, k)
+
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_baseline = run_cpu_baseline(a, sfa, b, sfb, m, n, k)
@@ -596,12 +604,70 @@ def bench_cutex(args):
         }
         if allgather is not None:
             line["allgather"] = allgather
+        if cublaslt is not None:
+            line["cublaslt"] = cublaslt
         print(json.dumps(line), flush=True)
 
     del graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def compare_cublaslt(args, a, sfa, b, sfb, d, graph, step, stream, m, n, k):
+    """cuBLASLt's MXFP8 GEMM (torch._scaled_mm) on the same device operands.
+
+    Each round replays one CUDA graph of `steps` launches of this kernel, then one
+    of cuBLASLt, after 0.3 s idle each; the medians over the rounds are reported
+    with the outputs' bitwise agreement."""
+    import torch
+
+    A, B = a.view(torch.float8_e4m3fn), b.view(torch.float8_e4m3fn)
+    SA, SB = sfa.view(torch.float8_e8m0fnu), sfb.view(torch.float8_e8m0fnu)
+    try:
+        with torch.cuda.stream(stream):
+            ref = torch._scaled_mm(A, B.t(), SA, SB, out_dtype=torch.bfloat16)
+            for _ in range(max(args.warmup, 3)):
+                torch._scaled_mm(A, B.t(), SA, SB, out_dtype=torch.bfloat16)
+            step()
+        torch.cuda.synchronize()
+    except RuntimeError as exc:  # e.g. a scale shape cuBLASLt does not take
+        return {"unavailable": str(exc).splitlines()[0][:200]}
+    equal = bool(torch.equal(ref.view(torch.int16), d.view(torch.int16)))
+    lt_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(lt_graph, stream=stream):
+        for _ in range(args.steps):
+            torch._scaled_mm(A, B.t(), SA, SB, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+
+    def timed(replay):
+        time.sleep(0.3)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            s0.record(stream)
+            replay()
+            s1.record(stream)
+        torch.cuda.synchronize()
+        return s0.elapsed_time(s1) / args.steps
+
+    def ours():
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(args.steps):
+                step()
+
+    mine, theirs = [], []
+    for _ in range(args.vs_cublaslt):
+        mine.append(timed(ours))
+        theirs.append(timed(lt_graph.replay))
+    del lt_graph
+    flops = 2.0 * m * n * k
+    med = lambda xs: sorted(xs)[len(xs) // 2]  # noqa: E731
+    return {"value": flops / (med(theirs) / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_launch": med(theirs),
+            "cutex_value_same_rounds": flops / (med(mine) / 1e3) / 1e12, "cutex_ms_per_launch": med(mine),
+            "rounds": args.vs_cublaslt, "bitwise_equal": equal,
+            "path": "torch._scaled_mm (cuBLASLt MXFP8, E4M3 x E4M3, E8M0 1x32 scales -> BF16), CUDA graph"}
 
 
 def measure_fp8_peak(args):
