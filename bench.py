@@ -178,6 +178,7 @@ class ClockSampler:
             "sm_mhz": statistics.median(sm) if sm else None,
             "sm_max_mhz": max(smax) if smax else None,
             "power_w_max": max(power) if power else None,
+            "power_w_median": statistics.median(power) if power else None,
             "reasons": sorted(reasons),
             "samples": len(sm),
         }
@@ -661,12 +662,32 @@ def compare_cublaslt(args, a, sfa, b, sfb, d, graph, step, stream, m, n, k):
     for _ in range(args.vs_cublaslt):
         mine.append(timed(ours))
         theirs.append(timed(lt_graph.replay))
+    sustained = None
+    if args.sustained_s > 0:
+        # The same back-to-back protocol as this kernel's `sustained` entry.
+        time.sleep(1.0)
+        sampler = ClockSampler(physical_gpu_index(0))
+        sampler.start()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches = 0
+        t_wall = time.time()
+        with torch.cuda.stream(stream):
+            s2.record(stream)
+            while time.time() - t_wall < args.sustained_s:
+                lt_graph.replay()
+                launches += args.steps
+                stream.synchronize()
+            e2.record(stream)
+        torch.cuda.synchronize()
+        secs = s2.elapsed_time(e2) / 1e3
+        sustained = {"value": 2.0 * m * n * k * launches / secs / 1e12, "unit": "TFLOP/s", "launches": launches,
+                     "seconds": secs, "clocks": sampler.stop()}
     del lt_graph
     flops = 2.0 * m * n * k
     med = lambda xs: sorted(xs)[len(xs) // 2]  # noqa: E731
     return {"value": flops / (med(theirs) / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_launch": med(theirs),
             "cutex_value_same_rounds": flops / (med(mine) / 1e3) / 1e12, "cutex_ms_per_launch": med(mine),
-            "rounds": args.vs_cublaslt, "bitwise_equal": equal,
+            "rounds": args.vs_cublaslt, "bitwise_equal": equal, "sustained": sustained,
             "path": "torch._scaled_mm (cuBLASLt MXFP8, E4M3 x E4M3, E8M0 1x32 scales -> BF16), CUDA graph"}
 
 
