@@ -250,7 +250,8 @@ class HostGemm:
         plan = query(m, n, k, self.config)
         self.workspace = None
         if plan["workspace_bytes"] > 0:
-            self.workspace = torch.empty(plan["workspace_bytes"], dtype=u8, device=dev)
+            # Zeroed: the arrival counters must start at zero (every launch leaves them so).
+            self.workspace = torch.zeros(plan["workspace_bytes"], dtype=u8, device=dev)
 
     @staticmethod
     def _host(t, shape_bytes: int, name: str) -> int:
