@@ -12,8 +12,10 @@ steps. ``value`` = 2*M*N*K*steps / (max over ranks of the device time of the
 timed region). ``e2e`` repeats the measurement from pinned host buffers, inside the
 CUDA-event timed interval: on 1 GPU through the library's host-buffer entry
 (``cutex_mxfp8_gemm_host``: A, B, SFA, SFB in, D out, copies and block GEMMs
-overlapped); on N GPUs through ``ShardedHostGemm`` (each rank copies 1/N of A and
-its B slice in, A is all-gathered over NVLink, D slices come back in row blocks).
+overlapped; independent steps alternate over ``--e2e-streams`` streams so one
+step's D2H overlaps the next step's H2D); on N GPUs through ``ShardedHostGemm``
+(each rank copies 1/N of A and its B slice in, A is all-gathered over NVLink,
+D slices come back in row blocks).
 
 ``--impl reference`` times the contract's CPU path (dequantise, fp32 matmul,
 cast to BF16: the oracle port) on the host cores, on bounded row/column
@@ -51,7 +53,10 @@ def parse_args():
     p.add_argument("--m", type=int, default=16384)
     p.add_argument("--n", type=int, default=16384)
     p.add_argument("--k", type=int, default=16384)
-    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--e2e-steps", type=int, default=6)
+    p.add_argument("--e2e-streams", type=int, default=2,
+                   help="N = 1: independent steps alternate over this many streams, each with its own HostGemm "
+                        "(device buffers) and pinned result, so one step's D2H overlaps the next step's H2D")
     p.add_argument("--e2e-blocks", type=int, default=4,
                    help="host pipeline: output cut into up to BxB blocks (copies and GEMMs overlapped)")
     p.add_argument("--allgather", action="store_true",
@@ -449,15 +454,26 @@ def bench_cutex(args):
             # copies overlapped on its own streams, joined back into `stream`.
             ha = a.cpu().pin_memory()
             hsa = sfa.cpu().pin_memory()
-            host_gemm = HostGemm(m, n_local, k, device=device, config=cfg, blocks=args.e2e_blocks)
+            # Steps are independent requests: step i runs on stream i % S with its
+            # own HostGemm (device buffers) and its own pinned result, in stream
+            # order on that stream; the library's copy/compute streams are shared,
+            # so one step's D2H tail overlaps the next step's H2D.
+            n_streams = max(1, args.e2e_streams)
+            e2e_streams = [stream] + [torch.cuda.Stream(device) for _ in range(n_streams - 1)]
+            host_gemms = [HostGemm(m, n_local, k, device=device, config=cfg, blocks=args.e2e_blocks)
+                          for _ in range(n_streams)]
+            hds = [hd] + [torch.empty(d.shape, dtype=d.dtype).pin_memory() for _ in range(n_streams - 1)]
+            step_no = [0]
 
             def e2e_step():
-                host_gemm(ha, hb, hsa, hsb, hd, stream=stream)
+                j = step_no[0] % n_streams
+                step_no[0] += 1
+                host_gemms[j](ha, hb, hsa, hsb, hds[j], stream=e2e_streams[j])
 
             h2d = ha.numel() + hb.numel() + hsa.numel() + hsb.numel()
             d2h = hd.numel() * hd.element_size()
             path = (f"cutex_mxfp8_gemm_host C ABI (HostGemm, {args.e2e_blocks}x{args.e2e_blocks} blocks), "
-                    "pinned host A/B/SFA/SFB in, D out")
+                    f"pinned host A/B/SFA/SFB in, D out; steps alternate over {n_streams} stream(s)")
         else:
             from cutex_b200.sharding import ShardedHostGemm
 
@@ -470,6 +486,8 @@ def bench_cutex(args):
             ha = a[r0:r1].cpu().pin_memory()
             hsa = sfa[r0 * sf_row:r1 * sf_row].cpu().pin_memory()
 
+            e2e_streams = [stream]
+
             def e2e_step():
                 host_gemm(ha, hsa, hb, hsb, hd, stream=stream)
 
@@ -479,15 +497,20 @@ def bench_cutex(args):
                     "NCCL all-gather of A, D slice out in row blocks")
 
         with torch.cuda.stream(stream):
-            e2e_step()
+            for _ in range(len(e2e_streams)):
+                e2e_step()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             s2.record(stream)
+            for other in e2e_streams[1:]:
+                other.wait_event(s2)
             for _ in range(args.e2e_steps):
                 e2e_step()
+            for other in e2e_streams[1:]:
+                stream.wait_stream(other)
             e2.record(stream)
         torch.cuda.synchronize()
         te = torch.tensor([s2.elapsed_time(e2)], dtype=torch.float64, device=device)
@@ -501,7 +524,11 @@ def bench_cutex(args):
             "steps": args.e2e_steps,
             "path": path,
         }
-        del host_gemm, ha, hb, hsa, hsb, hd
+        del ha, hb, hsa, hsb, hd
+        if world == 1:
+            del host_gemms, hds
+        else:
+            del host_gemm
 
     allgather = None
     if args.allgather and world > 1:
