@@ -69,6 +69,9 @@ def parse_args():
     p.add_argument("--vs-cublaslt", type=int, default=0, metavar="ROUNDS",
                    help="N = 1: also time cuBLASLt MXFP8 (torch._scaled_mm) on the same operands, alternating "
                         "ROUNDS graph replays of each with this kernel's, and compare the outputs bitwise")
+    p.add_argument("--quantize", choices=("rowwise", "columnwise"), default=None,
+                   help="N = 1: time the MXFP8 quantiser on an [M, K] input instead of the GEMM (GB/s vs HBM)")
+    p.add_argument("--qdtype", choices=("f32", "bf16"), default="f32", help="quantiser input type")
     p.add_argument("--measure-fp8-peak", action="store_true",
                    help="measure cuBLASLt MXFP8 (torch._scaled_mm) 8192^3: best-of-10 burst and 4 s sustained")
     p.add_argument("--dist", choices=("square", "llm"), default="square",
@@ -718,6 +721,79 @@ def compare_cublaslt(args, a, sfa, b, sfb, d, graph, step, stream, m, n, k):
             "path": "torch._scaled_mm (cuBLASLt MXFP8, E4M3 x E4M3, E8M0 1x32 scales -> BF16), CUDA graph"}
 
 
+def bench_quantize(args):
+    """The MXFP8 quantisers (the step before the GEMM) on an [M, K] input, device-timed.
+
+    Rowwise: x [M, K] -> E4M3 [M, K] + 1x32 E8M0 scales along K (128x4 layout).
+    Columnwise: x [M, K] -> E4M3 [K, M] = quantise(x^T) + scales of a [K, M]
+    operand. Algorithmic bytes per launch: M*K*(input bytes + 1) + M*K/32; one CUDA
+    graph of `steps` launches; the 1 GB (f32) or 512 MB (bf16) input exceeds the L2."""
+    import torch
+
+    from cutex_b200.kernels import quantize_mxfp8, quantize_mxfp8_columnwise
+    from cutex_b200.kernels.dense_gemm import scale_buffer_bytes
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    m, k = args.m, args.k
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    x = torch.randn(m, k, device=dev, generator=g)
+    x *= torch.exp2(torch.empty(m, 1, device=dev).uniform_(-4.0, 4.0, generator=g))
+    if args.qdtype == "bf16":
+        x = x.to(torch.bfloat16)
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    if args.quantize == "rowwise":
+        q = torch.empty(m, k, dtype=torch.uint8, device=dev)
+        sf = torch.empty(scale_buffer_bytes(m, k), dtype=torch.uint8, device=dev)
+        step = lambda: quantize_mxfp8(x, q=q, sf=sf, stream=stream)  # noqa: E731
+    else:
+        q = torch.empty(k, m, dtype=torch.uint8, device=dev)
+        sf = torch.empty(scale_buffer_bytes(k, m), dtype=torch.uint8, device=dev)
+        step = lambda: quantize_mxfp8_columnwise(x, qt=q, sft=sf, stream=stream)  # noqa: E731
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(args.steps):
+            step()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(physical_gpu_index(0))
+    sampler.start()
+    time.sleep(0.3)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        s0.record(stream)
+        graph.replay()
+        s1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = s0.elapsed_time(s1) / args.steps
+    in_bytes = 4 if args.qdtype == "f32" else 2
+    nbytes = float(m * k * (in_bytes + 1) + m * k // 32)
+    peaks, source = load_peaks()
+    achieved = nbytes / (ms / 1e3) / 1e9
+    peak = float(peaks["hbm_gbs"])
+    print(json.dumps({
+        "metric": f"MXFP8 {args.quantize} quantiser GB/s (device-timed)",
+        "value": achieved, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "dtype": f"{args.qdtype}->e4m3+e8m0", "data": "synthetic",
+        "config": {"workload": f"mxfp8_quantize_{args.quantize}_{args.qdtype}_m{m}_k{k}", "m": m, "k": k,
+                   "l2": "no flush: the input exceeds the 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_source": f"{source} HBM copy (hbm_gbs)",
+                     "algorithmic_bytes_per_launch": nbytes, "launch_avg_ms": ms},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }), flush=True)
+    del graph
+
+
 def measure_fp8_peak(args):
     """Dense FP8 denominator measured like the driver's BF16 peak: the vendor library on 8192^3.
 
@@ -775,6 +851,9 @@ def main():
     args = parse_args()
     if args.measure_fp8_peak:
         measure_fp8_peak(args)
+        return
+    if args.quantize is not None:
+        bench_quantize(args)
         return
     if args.impl == "reference":
         bench_reference(args)

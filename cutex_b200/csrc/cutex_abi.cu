@@ -825,12 +825,12 @@ extern "C" int cutex_mxfp8_quantize_columnwise(const void* x, int32_t x_dtype, i
   if (x_dtype != 0 && x_dtype != 1) return CUTEX_ERR_INVALID_ARGUMENT;
   if (rows < 1 || cols < 1 || rows > kMaxDim || cols > kMaxDim) return CUTEX_ERR_SHAPE;
   if (rows % 128 != 0 || ldx < cols || ldx % 8 != 0) return CUTEX_ERR_ALIGN;
-  if (rows / 128 > 65535) return CUTEX_ERR_SHAPE;  // grid.y: one CTA row per 128 rows of x
   if (!aligned16(x) || !aligned16(qt) || !aligned16(sft)) return CUTEX_ERR_ALIGN;
   DeviceState* ds = nullptr;
   const int st = current_device_state(&ds);
   if (st != CUTEX_OK) return st;
-  return launch_quantize_columnwise(x, x_dtype, rows, cols, ldx, qt, sft, reinterpret_cast<cudaStream_t>(stream))
+  return launch_quantize_columnwise(x, x_dtype, rows, cols, ldx, qt, sft, ds->sm_count,
+                                    reinterpret_cast<cudaStream_t>(stream))
              ? CUTEX_OK
              : CUTEX_ERR_CUDA;
 }

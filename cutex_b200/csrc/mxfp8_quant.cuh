@@ -10,8 +10,10 @@
 //
 // HBM-bound: four threads share one 32-element block (8 elements each, 16 or
 // 32 bytes per thread per load), a warp covers 256 contiguous elements of a
-// row, and the grid strides over [rows_padded x K/8]. Padding rows of the last
-// 128-row scale block get scale 0x00 and no element writes.
+// row. A CTA walks whole rows (grid-stride over the padded rows) and its
+// threads stride along the row, so no index needs a division; the row loop is
+// unrolled so each thread has several loads in flight. Padding rows of the
+// last 128-row scale block get scale 0x00 and no element writes.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -29,77 +31,176 @@ __device__ __forceinline__ uint32_t fp8x2(float lo, float hi) {
   return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3));
 }
 
+// Raw words of one 8-element group: 8 fp32 or 4 bf16x2.
+template <int kDtype>
+struct GroupRaw {
+  uint32_t w[kDtype == 0 ? 8 : 4];
+};
+
+// Loads group g of row r (zeros for a padding row r >= rows).
+template <int kDtype>
+__device__ __forceinline__ void load_group(const void* __restrict__ x, int64_t rows, int64_t ldx, int64_t r,
+                                           int64_t g, GroupRaw<kDtype>& raw) {
+  if (r < rows) {
+    if constexpr (kDtype == 0) {
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(x) + r * ldx + g * 8);
+      const uint4 a = __ldcs(p);
+      const uint4 b = __ldcs(p + 1);
+      raw.w[0] = a.x; raw.w[1] = a.y; raw.w[2] = a.z; raw.w[3] = a.w;
+      raw.w[4] = b.x; raw.w[5] = b.y; raw.w[6] = b.z; raw.w[7] = b.w;
+    } else {
+      const uint4 a =
+          __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + r * ldx + g * 8));
+      raw.w[0] = a.x; raw.w[1] = a.y; raw.w[2] = a.z; raw.w[3] = a.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < (kDtype == 0 ? 8 : 4); ++j) raw.w[j] = 0u;
+  }
+}
+
+// The 8 fp32 values of a loaded group.
+template <int kDtype>
+__device__ __forceinline__ void unpack_group(const GroupRaw<kDtype>& raw, float (&v)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if constexpr (kDtype == 0)
+      v[j] = __uint_as_float(raw.w[j]);
+    else
+      v[j] = __uint_as_float(j % 2 == 0 ? raw.w[j / 2] << 16 : raw.w[j / 2] & 0xFFFF0000u);
+  }
+}
+
+// Quantises group g of row r (values v) and stores its codes and, from the
+// quad's first lane, the block's scale byte. The four lanes of a quad hold one
+// 1x32 block; `quad` is their lane mask.
+__device__ __forceinline__ void finish_group(const float (&v)[8], int64_t rows, int64_t K, uint8_t* __restrict__ q,
+                                             uint8_t* __restrict__ sf, int64_t r, int64_t g, unsigned quad) {
+  // amax on the magnitude bit patterns: for non-negative floats integer order is
+  // value order, and a NaN or infinity (bits >= 0x7F800000) is the maximum.
+  uint32_t amax = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) amax = max(amax, __float_as_uint(v[j]) & 0x7FFFFFFFu);
+  amax = max(amax, __shfl_xor_sync(quad, amax, 1));
+  amax = max(amax, __shfl_xor_sync(quad, amax, 2));
+  const bool nonfinite = amax >= 0x7F800000u;
+  const uint32_t exp_field = amax >> 23;
+  const uint32_t sbyte = nonfinite ? 0xFFu : (exp_field >= 8u ? exp_field - 8u : 0u);
+  if (r < rows) {
+    uint2 out = make_uint2(0u, 0u);
+    if (!nonfinite) {
+      const float mult = __uint_as_float((254u - sbyte) << 23);  // 2^(127 - sbyte), exact
+      out.x = fp8x2(v[0] * mult, v[1] * mult) | (fp8x2(v[2] * mult, v[3] * mult) << 16);
+      out.y = fp8x2(v[4] * mult, v[5] * mult) | (fp8x2(v[6] * mult, v[7] * mult) << 16);
+    }
+    *reinterpret_cast<uint2*>(q + r * K + g * 8) = out;
+  }
+  if ((g & 3) == 0) {
+    // sf_offset(r, c = g / 4, K) with the row's part hoisted: 512-byte chunk
+    // (r / 128, c / 4), byte (r % 32) * 16 + (r % 128 / 32) * 4 + c % 4.
+    const int64_t row_part = ((r >> 7) * (K >> 7)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4;
+    const uint32_t c = static_cast<uint32_t>(g) >> 2;
+    sf[row_part + ((c >> 2) << 9) + (c & 3u)] = static_cast<uint8_t>(sbyte);
+  }
+}
+
 template <int kDtype>  // 0: float32, 1: bfloat16
 __global__ void __launch_bounds__(256) mxfp8_quantize_kernel(const void* __restrict__ x, int64_t rows,
                                                              int64_t K, int64_t ldx,
                                                              uint8_t* __restrict__ q,
                                                              uint8_t* __restrict__ sf) {
-  const int64_t k8 = K >> 3;  // 8-element groups per row
+  const int64_t k8 = K >> 3;  // 8-element groups per row (a multiple of 16)
   const int64_t rows_pad = (rows + 127) & ~int64_t{127};
-  const int64_t total = rows_pad * k8;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  // Trip count is uniform across each group of 4 lanes (total % 4 == 0 and the
-  // start index is a multiple of 4 apart within a quad), so the shuffles below
-  // always see their partner lanes.
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int64_t r = i / k8;
-    const int64_t g = i - r * k8;  // 8-element group within the row
-    float v[8];
-    if (r < rows) {
-      if constexpr (kDtype == 0) {
-        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + r * ldx + g * 8);
-        const float4 a = __ldcs(p);
-        const float4 b = __ldcs(p + 1);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      } else {
-        const uint4 a = __ldcs(reinterpret_cast<const uint4*>(
-            static_cast<const __nv_bfloat16*>(x) + r * ldx + g * 8));
-        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+  // blockDim.x and k8 are multiples of 4, so the four lanes of a quad always
+  // take the same trip through the row loop.
+  const unsigned quad = 0xFu << (threadIdx.x & 28u);
+  if constexpr (kDtype == 1) {
+    // bf16: 4 groups (64 bytes) per thread and step, software-pipelined: the
+    // next step's loads are issued before the current step is quantised, so
+    // each thread's arithmetic overlaps its own loads.
+    constexpr int kP = 4;
+    const int64_t pstep = static_cast<int64_t>(blockDim.x) * kP;
+    int64_t r = blockIdx.x, g0 = threadIdx.x;
+    bool have = r < rows_pad && g0 < k8;
+    GroupRaw<kDtype> cur[kP];
+    auto load_step = [&](int64_t rr, int64_t gg, GroupRaw<kDtype>(&dst)[kP]) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          v[2 * j] = __uint_as_float(w[j] << 16);
-          v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+      for (int u = 0; u < kP; ++u) {
+        const int64_t g = gg + u * static_cast<int64_t>(blockDim.x);
+        if (g < k8) load_group<kDtype>(x, rows, ldx, rr, g, dst[u]);
+      }
+    };
+    if (have) load_step(r, g0, cur);
+    while (have) {
+      int64_t nr = r, ng = g0 + pstep;
+      if (ng >= k8) {
+        ng = threadIdx.x;
+        nr = r + gridDim.x;
+      }
+      const bool nhave = nr < rows_pad;
+      GroupRaw<kDtype> nxt[kP];
+      if (nhave) load_step(nr, ng, nxt);
+#pragma unroll
+      for (int u = 0; u < kP; ++u) {
+        const int64_t g = g0 + u * static_cast<int64_t>(blockDim.x);
+        if (g < k8) {
+          float v[8];
+          unpack_group<kDtype>(cur[u], v);
+          finish_group(v, rows, K, q, sf, r, g, quad);
         }
       }
-    } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      for (int u = 0; u < kP; ++u) cur[u] = nxt[u];
+      r = nr;
+      g0 = ng;
+      have = nhave;
     }
-    float amax = 0.f;
-    uint32_t nonfinite = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t bits = __float_as_uint(v[j]) & 0x7FFFFFFFu;
-      nonfinite |= bits >= 0x7F800000u ? 1u : 0u;
-      amax = fmaxf(amax, __uint_as_float(bits));
-    }
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
-    nonfinite |= __shfl_xor_sync(0xFFFFFFFFu, nonfinite, 1);
-    nonfinite |= __shfl_xor_sync(0xFFFFFFFFu, nonfinite, 2);
-    const uint32_t exp_field = __float_as_uint(amax) >> 23;
-    const uint32_t sbyte = nonfinite ? 0xFFu : (exp_field >= 8u ? exp_field - 8u : 0u);
-    if (r < rows) {
-      uint2 out = make_uint2(0u, 0u);
-      if (!nonfinite) {
-        const float mult = __uint_as_float((254u - sbyte) << 23);  // 2^(127 - sbyte), exact
-        out.x = fp8x2(v[0] * mult, v[1] * mult) | (fp8x2(v[2] * mult, v[3] * mult) << 16);
-        out.y = fp8x2(v[4] * mult, v[5] * mult) | (fp8x2(v[6] * mult, v[7] * mult) << 16);
-      }
-      *reinterpret_cast<uint2*>(q + r * K + g * 8) = out;
-    }
-    if ((g & 3) == 0) sf[sf_offset(r, g >> 2, K)] = static_cast<uint8_t>(sbyte);
+    return;
   }
+  // fp32: kU groups per thread and step, all loaded (as raw words, 32
+  // registers) before any is quantised: 128 bytes of loads in flight per thread.
+  constexpr int kU = 4;
+  const int64_t step = static_cast<int64_t>(blockDim.x) * kU;
+  for (int64_t r = blockIdx.x; r < rows_pad; r += gridDim.x) {
+    for (int64_t g0 = threadIdx.x; g0 < k8; g0 += step) {
+      GroupRaw<kDtype> raw[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t g = g0 + u * static_cast<int64_t>(blockDim.x);
+        if (g < k8) load_group<kDtype>(x, rows, ldx, r, g, raw[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t g = g0 + u * static_cast<int64_t>(blockDim.x);
+        if (g < k8) {
+          float v[8];
+          unpack_group<kDtype>(raw[u], v);
+          finish_group(v, rows, K, q, sf, r, g, quad);
+        }
+      }
+    }
+  }
+}
+
+// CTAs of `kernel` resident per SM at `threads` threads and `smem` bytes
+// (queried once per kernel; 1 if the query fails).
+inline int resident_ctas(const void* kernel, int threads, size_t smem) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) n = 1;
+  return n;
 }
 
 inline bool launch_quantize(const void* x, int dtype, int64_t rows, int64_t K, int64_t ldx, void* q,
                             void* sf, int sm_count, cudaStream_t stream) {
   const int64_t rows_pad = (rows + 127) & ~int64_t{127};
-  const int64_t total = rows_pad * (K >> 3);
-  const int threads = 256;
-  int64_t blocks = (total + threads - 1) / threads;
-  blocks = blocks < int64_t{sm_count} * 8 ? blocks : int64_t{sm_count} * 8;
+  const int64_t k8 = K >> 3;
+  // Whole rows per CTA; threads along the row (a multiple of 32, at most 256).
+  // One wave of resident CTAs, each walking a strided set of rows.
+  const int threads = static_cast<int>(k8 >= 256 ? 256 : ((k8 + 31) / 32) * 32);
+  static const int per_sm[2] = {resident_ctas(reinterpret_cast<const void*>(&mxfp8_quantize_kernel<0>), 256, 0),
+                                resident_ctas(reinterpret_cast<const void*>(&mxfp8_quantize_kernel<1>), 256, 0)};
+  const int64_t wave = int64_t{sm_count} * per_sm[dtype == 0 ? 0 : 1];
+  int64_t blocks = rows_pad < wave ? rows_pad : wave;
   if (blocks < 1) blocks = 1;
   if (dtype == 0)
     mxfp8_quantize_kernel<0><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
@@ -126,97 +227,141 @@ inline bool launch_quantize(const void* x, int dtype, int64_t rows, int64_t K, i
 constexpr int kColTileRows = 128;
 constexpr int kColTileCols = 64;
 
-template <int kDtype>  // 0: float32, 1: bfloat16
-__global__ void __launch_bounds__(256) mxfp8_quantize_columnwise_kernel(const void* __restrict__ x, int64_t rows,
-                                                                        int64_t cols, int64_t ldx,
-                                                                        uint8_t* __restrict__ qt,
-                                                                        uint8_t* __restrict__ sft) {
-  __shared__ float tile[kColTileRows][kColTileCols + 1];
-  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kColTileCols;
-  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kColTileRows;
-  const int t = threadIdx.x;
-  // Load: 8 consecutive columns per thread, 8 threads per row, 32 rows per pass.
+// This thread's 4 x 8 values of a 128 x 64 tile at (r0, c0): pass p covers tile
+// row 32p + t / 8, columns 8 (t % 8) .. + 7 (zeros past `cols`), kept as raw
+// words (8 fp32 or 4 bf16x2 per pass) until they are written to SMEM.
+template <int kDtype>
+struct ColRaw {
+  uint32_t w[4][kDtype == 0 ? 8 : 4];
+};
+
+template <int kDtype>
+__device__ __forceinline__ void col_tile_load(const void* __restrict__ x, int64_t cols, int64_t ldx, int64_t r0,
+                                              int64_t c0, int t, ColRaw<kDtype>& raw) {
   const int lc = (t & 7) * 8;
+  const int64_t c = c0 + lc;
 #pragma unroll
   for (int pass = 0; pass < 4; ++pass) {
-    const int lr = pass * 32 + (t >> 3);
-    const int64_t c = c0 + lc;
-    float v[8];
+    const int64_t row = r0 + pass * 32 + (t >> 3);
     if (c + 8 <= cols) {
       if constexpr (kDtype == 0) {
-        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + (r0 + lr) * ldx + c);
-        const float4 a = __ldcs(p);
-        const float4 b = __ldcs(p + 1);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(x) + row * ldx + c);
+        const uint4 a = __ldcs(p);
+        const uint4 b = __ldcs(p + 1);
+        raw.w[pass][0] = a.x; raw.w[pass][1] = a.y; raw.w[pass][2] = a.z; raw.w[pass][3] = a.w;
+        raw.w[pass][4] = b.x; raw.w[pass][5] = b.y; raw.w[pass][6] = b.z; raw.w[pass][7] = b.w;
       } else {
-        const uint4 a = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) +
-                                                             (r0 + lr) * ldx + c));
-        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          v[2 * j] = __uint_as_float(w[j] << 16);
-          v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
-        }
+        const uint4 a = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + row * ldx + c));
+        raw.w[pass][0] = a.x; raw.w[pass][1] = a.y; raw.w[pass][2] = a.z; raw.w[pass][3] = a.w;
       }
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float e = 0.f;
+        uint32_t e = 0u;
         if (c + j < cols) {
-          if constexpr (kDtype == 0) {
-            e = static_cast<const float*>(x)[(r0 + lr) * ldx + c + j];
-          } else {
-            const uint16_t h = reinterpret_cast<const uint16_t*>(x)[(r0 + lr) * ldx + c + j];
-            e = __uint_as_float(static_cast<uint32_t>(h) << 16);
-          }
+          if constexpr (kDtype == 0)
+            e = reinterpret_cast<const uint32_t*>(x)[row * ldx + c + j];
+          else
+            e = reinterpret_cast<const uint16_t*>(x)[row * ldx + c + j];
         }
-        v[j] = e;
+        if constexpr (kDtype == 0) {
+          raw.w[pass][j] = e;
+        } else {
+          if (j % 2 == 0) raw.w[pass][j / 2] = e;
+          else raw.w[pass][j / 2] |= e << 16;
+        }
       }
     }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) tile[lr][lc + j] = v[j];
   }
-  __syncthreads();
-  const int warp = t >> 5, lane = t & 31;
-  const int blk = warp & 3;                          // 32-row block of the tile
-  const int lcol = (warp >> 2) * 32 + lane;          // column within the tile
-  const int64_t c = c0 + lcol;                       // output row of qt
-  float v[32];
-  float amax = 0.f;
-  uint32_t nonfinite = 0;
+}
+
+// Writes the raw words of col_tile_load into the SMEM tile as fp32.
+template <int kDtype>
+__device__ __forceinline__ void col_tile_store(const ColRaw<kDtype>& raw, float (*tile)[kColTileCols + 1], int t) {
+  const int lc = (t & 7) * 8;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    v[i] = tile[blk * 32 + i][lcol];
-    const uint32_t bits = __float_as_uint(v[i]) & 0x7FFFFFFFu;
-    nonfinite |= bits >= 0x7F800000u ? 1u : 0u;
-    amax = fmaxf(amax, __uint_as_float(bits));
-  }
-  const uint32_t exp_field = __float_as_uint(amax) >> 23;
-  const uint32_t sbyte = nonfinite ? 0xFFu : (exp_field >= 8u ? exp_field - 8u : 0u);
-  const int64_t cols_pad = (cols + 127) & ~int64_t{127};
-  if (c < cols) {
-    uint32_t w[8];
-    if (!nonfinite) {
-      const float mult = __uint_as_float((254u - sbyte) << 23);  // 2^(127 - sbyte), exact
+  for (int pass = 0; pass < 4; ++pass) {
+    float* dst = &tile[pass * 32 + (t >> 3)][lc];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        w[j] = fp8x2(v[4 * j] * mult, v[4 * j + 1] * mult) | (fp8x2(v[4 * j + 2] * mult, v[4 * j + 3] * mult) << 16);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) w[j] = 0u;
+    for (int j = 0; j < 8; ++j) {
+      if constexpr (kDtype == 0)
+        dst[j] = __uint_as_float(raw.w[pass][j]);
+      else
+        dst[j] = __uint_as_float(j % 2 == 0 ? raw.w[pass][j / 2] << 16 : raw.w[pass][j / 2] & 0xFFFF0000u);
     }
-    uint4* dst = reinterpret_cast<uint4*>(qt + c * rows + r0 + blk * 32);
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
   }
-  if (c < cols_pad) sft[sf_offset(c, (r0 >> 5) + blk, rows)] = static_cast<uint8_t>(c < cols ? sbyte : 0u);
+}
+
+template <int kDtype>  // 0: float32, 1: bfloat16
+__global__ void __launch_bounds__(256, 3) mxfp8_quantize_columnwise_kernel(const void* __restrict__ x, int64_t rows,
+                                                                        int64_t cols, int64_t ldx,
+                                                                        uint8_t* __restrict__ qt,
+                                                                        uint8_t* __restrict__ sft) {
+  __shared__ float tile[kColTileRows][kColTileCols + 1];
+  const int64_t cols_pad = (cols + 127) & ~int64_t{127};
+  const int64_t col_tiles = cols_pad / kColTileCols;
+  const int64_t num_tiles = col_tiles * (rows / kColTileRows);
+  const int t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31;
+  const int blk = warp & 3;                  // 32-row block of the tile
+  const int lcol = (warp >> 2) * 32 + lane;  // column within the tile
+  // Persistent: the CTA walks tiles blockIdx.x, + gridDim.x, ... (column tiles
+  // fastest, so neighbouring CTAs read neighbouring columns of the same rows);
+  // the next tile's loads are in flight (registers) while the current one is
+  // quantised from SMEM.
+  ColRaw<kDtype> nxt;
+  int64_t u = blockIdx.x;
+  if (u < num_tiles) col_tile_load<kDtype>(x, cols, ldx, (u / col_tiles) * kColTileRows, (u % col_tiles) * kColTileCols, t, nxt);
+  for (; u < num_tiles; u += gridDim.x) {
+    const int64_t r0 = (u / col_tiles) * kColTileRows;
+    const int64_t c = (u % col_tiles) * kColTileCols + lcol;  // output row of qt
+    __syncthreads();  // the previous tile's SMEM reads are done
+    col_tile_store<kDtype>(nxt, tile, t);
+    __syncthreads();
+    const int64_t un = u + gridDim.x;
+    if (un < num_tiles)
+      col_tile_load<kDtype>(x, cols, ldx, (un / col_tiles) * kColTileRows, (un % col_tiles) * kColTileCols, t, nxt);
+    float v[32];
+    uint32_t amax = 0u;  // magnitude bits: integer order is value order, NaN/inf the maximum
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      v[i] = tile[blk * 32 + i][lcol];
+      amax = max(amax, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+    }
+    const bool nonfinite = amax >= 0x7F800000u;
+    const uint32_t exp_field = amax >> 23;
+    const uint32_t sbyte = nonfinite ? 0xFFu : (exp_field >= 8u ? exp_field - 8u : 0u);
+    if (c < cols) {
+      uint32_t w[8];
+      if (!nonfinite) {
+        const float mult = __uint_as_float((254u - sbyte) << 23);  // 2^(127 - sbyte), exact
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          w[j] = fp8x2(v[4 * j] * mult, v[4 * j + 1] * mult) | (fp8x2(v[4 * j + 2] * mult, v[4 * j + 3] * mult) << 16);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = 0u;
+      }
+      uint4* dst = reinterpret_cast<uint4*>(qt + c * rows + r0 + blk * 32);
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    if (c < cols_pad) sft[sf_offset(c, (r0 >> 5) + blk, rows)] = static_cast<uint8_t>(c < cols ? sbyte : 0u);
+  }
 }
 
 inline bool launch_quantize_columnwise(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx, void* qt,
-                                       void* sft, cudaStream_t stream) {
+                                       void* sft, int sm_count, cudaStream_t stream) {
   const int64_t cols_pad = (cols + 127) & ~int64_t{127};
-  const dim3 grid(static_cast<unsigned>(cols_pad / kColTileCols), static_cast<unsigned>(rows / kColTileRows));
+  const int64_t num_tiles = (cols_pad / kColTileCols) * (rows / kColTileRows);
+  // One wave of resident CTAs, each walking a strided set of tiles.
+  static const int per_sm[2] = {
+      resident_ctas(reinterpret_cast<const void*>(&mxfp8_quantize_columnwise_kernel<0>), 256, 0),
+      resident_ctas(reinterpret_cast<const void*>(&mxfp8_quantize_columnwise_kernel<1>), 256, 0)};
+  const int64_t wave = int64_t{sm_count} * per_sm[dtype == 0 ? 0 : 1];
+  int64_t blocks = num_tiles < wave ? num_tiles : wave;
+  if (blocks < 1) blocks = 1;
+  const dim3 grid(static_cast<unsigned>(blocks));
   if (dtype == 0)
     mxfp8_quantize_columnwise_kernel<0><<<grid, 256, 0, stream>>>(x, rows, cols, ldx, static_cast<uint8_t*>(qt),
                                                                   static_cast<uint8_t*>(sft));
