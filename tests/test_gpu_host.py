@@ -51,7 +51,8 @@ def test_host_pipeline_equals_device_path(shape, blocks):
     # A second call on the same object (streams and events reused) with new data.
     a2, sfa2, b2, sfb2 = make_operands(M, N, K, seed=M + N + blocks + 1)
     hd2 = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
-    hg(_pinned(a2), _pinned(b2), _pinned(sfa2), _pinned(sfb2), hd2)
+    host2 = (_pinned(a2), _pinned(b2), _pinned(sfa2), _pinned(sfb2))  # alive until the copies have run
+    hg(*host2, hd2)
     torch.cuda.synchronize()
     ref2 = _device_result(a2, sfa2, b2, sfb2, M, N)
     assert torch.equal(hd2.view(torch.int16), ref2.view(torch.int16))
@@ -61,7 +62,8 @@ def test_host_pipeline_against_oracle():
     M, N, K = 768, 640, 1024
     a, sfa, b, sfb = make_operands(M, N, K, seed=5)
     hd = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
-    dense_gemm_host(_pinned(a), _pinned(b), _pinned(sfa), _pinned(sfb), hd, blocks=3)
+    host = (_pinned(a), _pinned(b), _pinned(sfa), _pinned(sfb))  # alive until the copies have run
+    dense_gemm_host(*host, hd, blocks=3)
     torch.cuda.synchronize()
     r = check(hd, a, sfa, b, sfb, M, N, K)
     assert r["ok"], r
@@ -93,3 +95,25 @@ def test_host_pipeline_rejects_bad_arguments():
         hg(small, good_a, good_a, good_a, torch.empty(256, 256, dtype=torch.bfloat16))
     with pytest.raises(_lib.CutexArgumentError):
         hg(good_a.cuda(), good_a, good_a, good_a, torch.empty(256, 256, dtype=torch.bfloat16))
+
+
+def test_independent_requests_on_two_streams():
+    # Two HostGemm objects (own device buffers) on two streams share the
+    # library's copy/compute streams: alternating calls overlap, and every
+    # result must still equal the device path bit for bit.
+    M, N, K = 1024, 1536, 512
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    gemms = [HostGemm(M, N, K, blocks=4), HostGemm(M, N, K, blocks=4)]
+    cases, outs, keep = [], [], []
+    for i in range(6):
+        a, sfa, b, sfb = make_operands(M, N, K, seed=100 + i)
+        cases.append((a, sfa, b, sfb))
+        host = (_pinned(a), _pinned(b), _pinned(sfa), _pinned(sfb))
+        keep.append(host)  # pinned inputs stay alive until the copies have run
+        hd = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        gemms[i % 2](*host, hd, stream=streams[i % 2])
+        outs.append(hd)
+    torch.cuda.synchronize()
+    for (a, sfa, b, sfb), hd in zip(cases, outs):
+        ref = _device_result(a, sfa, b, sfb, M, N)
+        assert torch.equal(hd.view(torch.int16), ref.view(torch.int16))
