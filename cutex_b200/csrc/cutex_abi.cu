@@ -13,6 +13,7 @@
 #include "../../include/cutex_mxfp8.h"
 #include "mxfp8_gemm.cuh"
 #include "mxfp8_quant.cuh"
+#include "mxfp8_quant_columnwise.cuh"
 #include "mxfp8_skinny.cuh"
 
 namespace cutex {
@@ -134,6 +135,50 @@ bool encode_output_fp8(CUtensorMap* map, void* p, int64_t M, int64_t N, int64_t 
   const uint32_t box[2] = {64u, 32u};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B,
                 CU_TENSOR_MAP_L2_PROMOTION_NONE);
+}
+
+// Columnwise quantiser input x [rows, cols] (fp32 or bf16, row stride ldx
+// elements) read in 128-row x 64-column boxes; columns past `cols` read as 0.
+bool encode_columnwise_input(CUtensorMap* map, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx) {
+  const uint64_t elem = dtype == 0 ? 4u : 2u;
+  const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ldx) * elem};
+  const uint32_t box[2] = {static_cast<uint32_t>(kColTileCols), static_cast<uint32_t>(kColTileRows)};
+  return encode(map, dtype == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims,
+                strides, box, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
+}
+
+// Columnwise quantiser output qt [cols, rows] e4m3 written in 64-row x
+// 128-byte boxes with a 128-byte swizzle; rows past `cols` are clipped.
+bool encode_columnwise_output(CUtensorMap* map, void* qt, int64_t rows, int64_t cols) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(rows), static_cast<uint64_t>(cols)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(rows)};
+  const uint32_t box[2] = {static_cast<uint32_t>(kColTileRows), static_cast<uint32_t>(kColTileCols)};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qt, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_NONE);
+}
+
+template <int kDtype>
+int launch_quantize_columnwise_t(const CUtensorMap& tmap, const CUtensorMap& tmap_qt, int64_t rows, int64_t cols,
+                                 void* sft, int sm_count, cudaStream_t stream) {
+  using C = ColCfg<kDtype>;
+  const void* fn = reinterpret_cast<const void*>(&mxfp8_quantize_columnwise_kernel<kDtype>);
+  static int per_sm = 0;  // resident CTAs per SM (one wave of persistent CTAs)
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (per_sm == 0) {
+      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
+        return CUTEX_ERR_CUDA;
+      per_sm = resident_ctas(fn, 256, C::kSmemBytes);
+    }
+  }
+  const int64_t cols_pad = (cols + 127) & ~int64_t{127};
+  const int64_t num_tiles = (cols_pad / kColTileCols) * (rows / kColTileRows);
+  const int64_t wave = int64_t{sm_count} * per_sm;
+  const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min(num_tiles, wave)));
+  mxfp8_quantize_columnwise_kernel<kDtype><<<blocks, 256, C::kSmemBytes, stream>>>(tmap, tmap_qt, rows, cols,
+                                                                                   static_cast<uint8_t*>(sft));
+  return cudaGetLastError() == cudaSuccess ? CUTEX_OK : CUTEX_ERR_CUDA;
 }
 
 // ------------------------------------------------------------ kernel registry
@@ -829,10 +874,12 @@ extern "C" int cutex_mxfp8_quantize_columnwise(const void* x, int32_t x_dtype, i
   DeviceState* ds = nullptr;
   const int st = current_device_state(&ds);
   if (st != CUTEX_OK) return st;
-  return launch_quantize_columnwise(x, x_dtype, rows, cols, ldx, qt, sft, ds->sm_count,
-                                    reinterpret_cast<cudaStream_t>(stream))
-             ? CUTEX_OK
-             : CUTEX_ERR_CUDA;
+  CUtensorMap tmap, tmap_qt;
+  if (!encode_columnwise_input(&tmap, x, x_dtype, rows, cols, ldx) || !encode_columnwise_output(&tmap_qt, qt, rows, cols))
+    return CUTEX_ERR_CUDA;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return x_dtype == 0 ? launch_quantize_columnwise_t<0>(tmap, tmap_qt, rows, cols, sft, ds->sm_count, s)
+                      : launch_quantize_columnwise_t<1>(tmap, tmap_qt, rows, cols, sft, ds->sm_count, s);
 }
 
 extern "C" const char* cutex_status_string(int status) {

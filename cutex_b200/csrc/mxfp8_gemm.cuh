@@ -51,6 +51,7 @@ enum DeviceError : int {
   kDevTimeoutEpilogue = 0x103,
   kDevTimeoutAccEmpty = 0x104,
   kDevTimeoutScheduler = 0x105,
+  kDevTimeoutQuantize = 0x106,  // columnwise quantiser: a TMA tile never arrived
   kDevBadTile = 0x201,  // a scheduled tile id outside [0, num_tiles): work stopped, nothing accessed
 };
 

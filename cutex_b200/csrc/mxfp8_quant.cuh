@@ -211,164 +211,4 @@ inline bool launch_quantize(const void* x, int dtype, int64_t rows, int64_t K, i
   return cudaGetLastError() == cudaSuccess;
 }
 
-// Columnwise quantiser: the operand layout a GEMM needs when the reduction
-// runs over the rows of x (weight gradients reduce over tokens; input
-// gradients read W along its columns). For x[rows, cols] it writes
-// qt[cols, rows] = quantise(x^T): 1x32 blocks run down the columns of x, and
-// the scales land in the 128x4 swizzled layout of a [cols, K = rows] operand.
-// Same per-block rule as the rowwise kernel.
-//
-// A CTA stages a 128-row x 64-column tile of x in shared memory (coalesced
-// 16/32-byte loads along the rows), then warp w quantises block w % 4 (rows
-// 32b..32b+31) of columns 32 (w / 4) .. + 31: one lane per column, so each
-// lane holds a whole 32-element block (no shuffles) and writes 32 contiguous
-// bytes of qt and one scale byte. Columns from cols up to the next multiple of
-// 128 (the scale layout's padding rows) get scale 0x00 and no element writes.
-constexpr int kColTileRows = 128;
-constexpr int kColTileCols = 64;
-
-// This thread's 4 x 8 values of a 128 x 64 tile at (r0, c0): pass p covers tile
-// row 32p + t / 8, columns 8 (t % 8) .. + 7 (zeros past `cols`), kept as raw
-// words (8 fp32 or 4 bf16x2 per pass) until they are written to SMEM.
-template <int kDtype>
-struct ColRaw {
-  uint32_t w[4][kDtype == 0 ? 8 : 4];
-};
-
-template <int kDtype>
-__device__ __forceinline__ void col_tile_load(const void* __restrict__ x, int64_t cols, int64_t ldx, int64_t r0,
-                                              int64_t c0, int t, ColRaw<kDtype>& raw) {
-  const int lc = (t & 7) * 8;
-  const int64_t c = c0 + lc;
-#pragma unroll
-  for (int pass = 0; pass < 4; ++pass) {
-    const int64_t row = r0 + pass * 32 + (t >> 3);
-    if (c + 8 <= cols) {
-      if constexpr (kDtype == 0) {
-        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(x) + row * ldx + c);
-        const uint4 a = __ldcs(p);
-        const uint4 b = __ldcs(p + 1);
-        raw.w[pass][0] = a.x; raw.w[pass][1] = a.y; raw.w[pass][2] = a.z; raw.w[pass][3] = a.w;
-        raw.w[pass][4] = b.x; raw.w[pass][5] = b.y; raw.w[pass][6] = b.z; raw.w[pass][7] = b.w;
-      } else {
-        const uint4 a = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + row * ldx + c));
-        raw.w[pass][0] = a.x; raw.w[pass][1] = a.y; raw.w[pass][2] = a.z; raw.w[pass][3] = a.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        uint32_t e = 0u;
-        if (c + j < cols) {
-          if constexpr (kDtype == 0)
-            e = reinterpret_cast<const uint32_t*>(x)[row * ldx + c + j];
-          else
-            e = reinterpret_cast<const uint16_t*>(x)[row * ldx + c + j];
-        }
-        if constexpr (kDtype == 0) {
-          raw.w[pass][j] = e;
-        } else {
-          if (j % 2 == 0) raw.w[pass][j / 2] = e;
-          else raw.w[pass][j / 2] |= e << 16;
-        }
-      }
-    }
-  }
-}
-
-// Writes the raw words of col_tile_load into the SMEM tile as fp32.
-template <int kDtype>
-__device__ __forceinline__ void col_tile_store(const ColRaw<kDtype>& raw, float (*tile)[kColTileCols + 1], int t) {
-  const int lc = (t & 7) * 8;
-#pragma unroll
-  for (int pass = 0; pass < 4; ++pass) {
-    float* dst = &tile[pass * 32 + (t >> 3)][lc];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if constexpr (kDtype == 0)
-        dst[j] = __uint_as_float(raw.w[pass][j]);
-      else
-        dst[j] = __uint_as_float(j % 2 == 0 ? raw.w[pass][j / 2] << 16 : raw.w[pass][j / 2] & 0xFFFF0000u);
-    }
-  }
-}
-
-template <int kDtype>  // 0: float32, 1: bfloat16
-__global__ void __launch_bounds__(256, 3) mxfp8_quantize_columnwise_kernel(const void* __restrict__ x, int64_t rows,
-                                                                        int64_t cols, int64_t ldx,
-                                                                        uint8_t* __restrict__ qt,
-                                                                        uint8_t* __restrict__ sft) {
-  __shared__ float tile[kColTileRows][kColTileCols + 1];
-  const int64_t cols_pad = (cols + 127) & ~int64_t{127};
-  const int64_t col_tiles = cols_pad / kColTileCols;
-  const int64_t num_tiles = col_tiles * (rows / kColTileRows);
-  const int t = threadIdx.x;
-  const int warp = t >> 5, lane = t & 31;
-  const int blk = warp & 3;                  // 32-row block of the tile
-  const int lcol = (warp >> 2) * 32 + lane;  // column within the tile
-  // Persistent: the CTA walks tiles blockIdx.x, + gridDim.x, ... (column tiles
-  // fastest, so neighbouring CTAs read neighbouring columns of the same rows);
-  // the next tile's loads are in flight (registers) while the current one is
-  // quantised from SMEM.
-  ColRaw<kDtype> nxt;
-  int64_t u = blockIdx.x;
-  if (u < num_tiles) col_tile_load<kDtype>(x, cols, ldx, (u / col_tiles) * kColTileRows, (u % col_tiles) * kColTileCols, t, nxt);
-  for (; u < num_tiles; u += gridDim.x) {
-    const int64_t r0 = (u / col_tiles) * kColTileRows;
-    const int64_t c = (u % col_tiles) * kColTileCols + lcol;  // output row of qt
-    __syncthreads();  // the previous tile's SMEM reads are done
-    col_tile_store<kDtype>(nxt, tile, t);
-    __syncthreads();
-    const int64_t un = u + gridDim.x;
-    if (un < num_tiles)
-      col_tile_load<kDtype>(x, cols, ldx, (un / col_tiles) * kColTileRows, (un % col_tiles) * kColTileCols, t, nxt);
-    float v[32];
-    uint32_t amax = 0u;  // magnitude bits: integer order is value order, NaN/inf the maximum
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      v[i] = tile[blk * 32 + i][lcol];
-      amax = max(amax, __float_as_uint(v[i]) & 0x7FFFFFFFu);
-    }
-    const bool nonfinite = amax >= 0x7F800000u;
-    const uint32_t exp_field = amax >> 23;
-    const uint32_t sbyte = nonfinite ? 0xFFu : (exp_field >= 8u ? exp_field - 8u : 0u);
-    if (c < cols) {
-      uint32_t w[8];
-      if (!nonfinite) {
-        const float mult = __uint_as_float((254u - sbyte) << 23);  // 2^(127 - sbyte), exact
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          w[j] = fp8x2(v[4 * j] * mult, v[4 * j + 1] * mult) | (fp8x2(v[4 * j + 2] * mult, v[4 * j + 3] * mult) << 16);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = 0u;
-      }
-      uint4* dst = reinterpret_cast<uint4*>(qt + c * rows + r0 + blk * 32);
-      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    }
-    if (c < cols_pad) sft[sf_offset(c, (r0 >> 5) + blk, rows)] = static_cast<uint8_t>(c < cols ? sbyte : 0u);
-  }
-}
-
-inline bool launch_quantize_columnwise(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx, void* qt,
-                                       void* sft, int sm_count, cudaStream_t stream) {
-  const int64_t cols_pad = (cols + 127) & ~int64_t{127};
-  const int64_t num_tiles = (cols_pad / kColTileCols) * (rows / kColTileRows);
-  // One wave of resident CTAs, each walking a strided set of tiles.
-  static const int per_sm[2] = {
-      resident_ctas(reinterpret_cast<const void*>(&mxfp8_quantize_columnwise_kernel<0>), 256, 0),
-      resident_ctas(reinterpret_cast<const void*>(&mxfp8_quantize_columnwise_kernel<1>), 256, 0)};
-  const int64_t wave = int64_t{sm_count} * per_sm[dtype == 0 ? 0 : 1];
-  int64_t blocks = num_tiles < wave ? num_tiles : wave;
-  if (blocks < 1) blocks = 1;
-  const dim3 grid(static_cast<unsigned>(blocks));
-  if (dtype == 0)
-    mxfp8_quantize_columnwise_kernel<0><<<grid, 256, 0, stream>>>(x, rows, cols, ldx, static_cast<uint8_t*>(qt),
-                                                                  static_cast<uint8_t*>(sft));
-  else
-    mxfp8_quantize_columnwise_kernel<1><<<grid, 256, 0, stream>>>(x, rows, cols, ldx, static_cast<uint8_t*>(qt),
-                                                                  static_cast<uint8_t*>(sft));
-  return cudaGetLastError() == cudaSuccess;
-}
-
 }  // namespace cutex
