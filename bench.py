@@ -57,6 +57,9 @@ def parse_args():
     p.add_argument("--e2e-streams", type=int, default=2,
                    help="N = 1: independent steps alternate over this many streams, each with its own HostGemm "
                         "(device buffers) and pinned result, so one step's D2H overlaps the next step's H2D")
+    p.add_argument("--e2e-sharded-streams", type=int, default=2,
+                   help="N > 1: the same alternation over this many streams, each ShardedHostGemm with its own "
+                        "process group (NCCL communicator) so that their all-gathers never share one")
     p.add_argument("--e2e-blocks", type=int, default=4,
                    help="host pipeline: output cut into up to BxB blocks (copies and GEMMs overlapped)")
     p.add_argument("--allgather", action="store_true",
@@ -483,21 +486,31 @@ def bench_cutex(args):
             # Each rank copies 1/world of A (A is the same on every rank) plus its
             # B slice in, NCCL gathers A over NVLink, D[:, n0:n1] comes back in row
             # blocks while the next block computes.
-            host_gemm = ShardedHostGemm(m, n, k, config=cfg, device=device)
+            # Steps alternate over S streams as on one GPU; each stream's
+            # ShardedHostGemm has its own process group, so two all-gathers in
+            # flight never share an NCCL communicator (every rank creates the
+            # groups and runs the steps in the same order).
+            n_streams = max(1, args.e2e_sharded_streams)
+            groups = [None] + [dist.new_group(backend="nccl") for _ in range(n_streams - 1)]
+            host_gemms = [ShardedHostGemm(m, n, k, group=g, config=cfg, device=device) for g in groups]
+            host_gemm = host_gemms[0]
             r0, r1 = host_gemm.rows.n0, host_gemm.rows.n1
             sf_row = k // 32
             ha = a[r0:r1].cpu().pin_memory()
             hsa = sfa[r0 * sf_row:r1 * sf_row].cpu().pin_memory()
-
-            e2e_streams = [stream]
+            e2e_streams = [stream] + [torch.cuda.Stream(device) for _ in range(n_streams - 1)]
+            hds = [hd] + [torch.empty(d.shape, dtype=d.dtype).pin_memory() for _ in range(n_streams - 1)]
+            step_no = [0]
 
             def e2e_step():
-                host_gemm(ha, hsa, hb, hsb, hd, stream=stream)
+                j = step_no[0] % n_streams
+                step_no[0] += 1
+                host_gemms[j](ha, hsa, hb, hsb, hds[j], stream=e2e_streams[j])
 
             h_in, h_out = host_gemm.host_bytes()
             h2d, d2h = h_in * world, h_out * world
             path = ("ShardedHostGemm: pinned host rows of A (1/world per rank) + B slice in, "
-                    "NCCL all-gather of A, D slice out in row blocks")
+                    f"NCCL all-gather of A, D slice out in row blocks; steps alternate over {n_streams} stream(s)")
 
         with torch.cuda.stream(stream):
             for _ in range(len(e2e_streams)):
@@ -527,11 +540,7 @@ def bench_cutex(args):
             "steps": args.e2e_steps,
             "path": path,
         }
-        del ha, hb, hsa, hsb, hd
-        if world == 1:
-            del host_gemms, hds
-        else:
-            del host_gemm
+        del ha, hb, hsa, hsb, hd, host_gemms, hds
 
     allgather = None
     if args.allgather and world > 1:
