@@ -15,7 +15,8 @@ CUDA-event timed interval: on 1 GPU through the library's host-buffer entry
 overlapped; independent steps alternate over ``--e2e-streams`` streams so one
 step's D2H overlaps the next step's H2D); on N GPUs through ``ShardedHostGemm``
 (each rank copies 1/N of A and its B slice in, A is all-gathered over NVLink,
-D slices come back in row blocks).
+D slices come back in row blocks; steps alternate over ``--e2e-sharded-streams``
+streams, each with its own process group).
 
 ``--impl reference`` times the contract's CPU path (dequantise, fp32 matmul,
 cast to BF16: the oracle port) on the host cores, on bounded row/column
