@@ -163,18 +163,24 @@ int launch_quantize_columnwise_t(const CUtensorMap& tmap, const CUtensorMap& tma
                                  void* sft, int sm_count, cudaStream_t stream) {
   using C = ColCfg<kDtype>;
   const void* fn = reinterpret_cast<const void*>(&mxfp8_quantize_columnwise_kernel<kDtype>);
-  static int per_sm = 0;  // resident CTAs per SM (one wave of persistent CTAs)
+  // Per device (the shared-memory attribute is set in each device's context):
+  // resident CTAs per SM, for one wave of persistent CTAs.
+  static int per_sm[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CUTEX_ERR_CUDA;
+  int resident = 0;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (per_sm == 0) {
+    if (per_sm[dev] == 0) {
       if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
         return CUTEX_ERR_CUDA;
-      per_sm = resident_ctas(fn, 256, C::kSmemBytes);
+      per_sm[dev] = resident_ctas(fn, 256, C::kSmemBytes);
     }
+    resident = per_sm[dev];
   }
   const int64_t cols_pad = (cols + 127) & ~int64_t{127};
   const int64_t num_tiles = (cols_pad / kColTileCols) * (rows / kColTileRows);
-  const int64_t wave = int64_t{sm_count} * per_sm;
+  const int64_t wave = int64_t{sm_count} * resident;
   const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min(num_tiles, wave)));
   mxfp8_quantize_columnwise_kernel<kDtype><<<blocks, 256, C::kSmemBytes, stream>>>(tmap, tmap_qt, rows, cols,
                                                                                    static_cast<uint8_t*>(sft));
