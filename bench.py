@@ -63,16 +63,20 @@ def parse_args():
                         "process group (NCCL communicator) so that their all-gathers never share one")
     p.add_argument("--e2e-blocks", type=int, default=4,
                    help="host pipeline: output cut into up to BxB blocks (copies and GEMMs overlapped)")
-    p.add_argument("--allgather", action="store_true",
-                   help="N > 1: also time gathering D on every rank, NCCL after the GEMM vs fused into it")
+    p.add_argument("--no-allgather", dest="allgather", action="store_false",
+                   help="N > 1: skip timing the gather of D on every rank (NCCL after the GEMM vs fused into it)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--config", type=str, default="", help="native config as JSON, e.g. '{\"kernel\": 2}'")
     p.add_argument("--no-graph", action="store_true", help="plain launches instead of one CUDA graph")
     p.add_argument("--sustained-s", type=float, default=2.0,
                    help="also run the launches back to back for this many seconds (0: skip)")
-    p.add_argument("--vs-cublaslt", type=int, default=0, metavar="ROUNDS",
+    p.add_argument("--vs-cublaslt", type=int, default=3, metavar="ROUNDS",
                    help="N = 1: also time cuBLASLt MXFP8 (torch._scaled_mm) on the same operands, alternating "
-                        "ROUNDS graph replays of each with this kernel's, and compare the outputs bitwise")
+                        "ROUNDS graph replays of each with this kernel's, and compare the outputs bitwise (0: skip)")
+    p.add_argument("--cublaslt-sustained", action="store_true",
+                   help="with --vs-cublaslt: also run cuBLASLt back to back for --sustained-s seconds")
+    p.add_argument("--no-configs", action="store_true",
+                   help="N = 1: skip the other BASELINE configurations timed beside the headline (`configs`)")
     p.add_argument("--quantize", choices=("rowwise", "columnwise"), default=None,
                    help="N = 1: time the MXFP8 quantiser on an [M, K] input instead of the GEMM (GB/s vs HBM)")
     p.add_argument("--qdtype", choices=("f32", "bf16"), default="f32", help="quantiser input type")
@@ -94,6 +98,19 @@ def workload_name(m, n, k):
     return f"mxfp8_fprop_m{m}_n{n}_k{k}"
 
 
+def workload_config(m, n, k, world, dist):
+    """The ``config`` object, identical in both arms (this library and ``--impl reference``)."""
+
+    return {
+        "workload": workload_name(m, n, k),
+        "m": m, "n": n, "k": k,
+        "parallelism": f"n-shard{world}" if world > 1 else "single",
+        "l2": "no flush: operands (E4M3 A + B slice + scales) exceed the 126 MB L2",
+        "inputs": ("N(0,1) x per-row 2^U(-4,4)" if dist == "square" else
+                   "activations N(0,1) with 0.1% of channels x50, weights N(0,0.02)") + ", OCP MX quantised, seed 0",
+    }
+
+
 def load_peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -105,18 +122,14 @@ def load_peaks():
 
 
 def fp8_peak(peaks, source, sustained):
-    """Dense FP8 tensor peak: a measured FP8 figure if one is recorded, else 2x the measured dense BF16."""
+    """Dense FP8 tensor-core denominator: 2 x the driver-measured dense BF16 rate (B200 FP8 = 2 x BF16).
 
-    fp8_file = PROFILES / "fp8_peak.json"
-    if fp8_file.exists():
-        try:
-            rec = json.loads(fp8_file.read_text())
-            key = "tflops_sustained" if sustained and "tflops_sustained" in rec else "tflops"
-            return float(rec[key]), f"measured FP8 ({rec.get('how', 'profiles/fp8_peak.json')}, {key})"
-        except (ValueError, KeyError):
-            pass
+    ``sustained`` selects the power-capped figure (a kernel timed inside a long
+    run) instead of the burst one. A vendor library's FP8 rate is a comparator,
+    reported as ``vs_cublaslt``, never a denominator."""
+
     key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
-    return 2.0 * float(peaks[key]), f"2 x {source} dense BF16 ({key}); FP8 dense rate is twice BF16 on B200"
+    return 2.0 * float(peaks[key]), f"2 x {source} dense BF16 ({key}) of MEASURED_PEAKS.json"
 
 
 def recorded_traffic(workload, n_gpus):
@@ -133,66 +146,119 @@ def recorded_traffic(workload, n_gpus):
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling in the background during the timed region."""
+    """Read-only NVML samples of SM clock, power and clock-event reasons every ``period_s``.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    ``mark()`` opens and ``close()`` ends the window that ``stop()`` summarises
+    (host ``perf_counter`` times bracketing the device-timed region: the host
+    enqueues the region's work after ``mark()`` and returns from the final
+    synchronisation before ``close()``), so a 60 ms region gets its own samples.
+    Without ``nvidia_ml_py`` it falls back to ``nvidia-smi -lms 200``. Nothing is
+    ever set through NVML.
+    """
 
-    def __init__(self, gpu_index: int):
+    REASONS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40), ("hw_power_brake_slowdown", 0x80))
+
+    def __init__(self, gpu_index: int, period_s: float = 0.01):
         self.gpu_index = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
-        self.thread = None
+        self.period_s = period_s
+        self.samples: list[tuple[float, float, float, float, int]] = []  # (t, sm MHz, max MHz, W, reasons)
+        self.window = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._smi = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu_index)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
-            return
-        self.thread = threading.Thread(target=self._read, daemon=True)
-        self.thread.start()
+            import pynvml
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
+        except Exception:  # no NVML binding or no driver: the nvidia-smi fallback
+            self._start_smi()
+            return self
+        reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        smax = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+
+        def run():
+            while not self._stop.is_set():
+                t = time.perf_counter()
+                try:
+                    sm = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                    watts = pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                    reasons = int(reasons_fn(handle))
+                except Exception:
+                    break
+                self.samples.append((t, sm, smax, watts, reasons))
+                self._stop.wait(self.period_s)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+        return self
+
+    def _start_smi(self):
+        fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.sw_power_cap,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown")
+        try:
+            self._smi = subprocess.Popen(["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu_index)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self._smi = None
+            return
+
+        def read():
+            for line in self._smi.stdout:
+                parts = [x.strip() for x in line.split(",")]
+                try:
+                    bits = sum(bit for (_, bit), v in zip(self.REASONS[:4], parts[3:7]) if v.lower() == "active")
+                    self.samples.append((time.perf_counter(), float(parts[0]), float(parts[1]), float(parts[2]), bits))
+                except (ValueError, IndexError):
+                    continue
+
+        self._thread = threading.Thread(target=read, daemon=True)
+        self._thread.start()
+        self.period_s = 0.2
+
+    def mark(self):
+        self.window = [time.perf_counter(), None]
+
+    def close(self):
+        if self.window is not None:
+            self.window[1] = time.perf_counter()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        if self.thread is not None:
-            self.thread.join(timeout=2)
-        sm, smax, power, reasons = [], [], [], set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
+        self._stop.set()
+        if self._smi is not None:
+            self._smi.terminate()
             try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-                power.append(float(parts[3]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
+                self._smi.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._smi.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        picked = self.samples
+        if self.window is not None and self.window[1] is not None:
+            t0, t1 = self.window
+            picked = [x for x in self.samples if t0 <= x[0] <= t1]
+        if not picked:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock samples"], "samples": 0,
+                    "source": "nvml" if self._smi is None else "nvidia-smi"}
+        reasons = sorted({name for _, _, _, _, bits in picked for name, bit in self.REASONS if bits & bit})
         return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": max(smax) if smax else None,
-            "power_w_max": max(power) if power else None,
-            "power_w_median": statistics.median(power) if power else None,
-            "reasons": sorted(reasons),
-            "samples": len(sm),
+            "sm_mhz": statistics.median(x[1] for x in picked),
+            "sm_mhz_min": min(x[1] for x in picked),
+            "sm_max_mhz": max(x[2] for x in picked),
+            "power_w_median": statistics.median(x[3] for x in picked),
+            "power_w_max": max(x[3] for x in picked),
+            "reasons": reasons,
+            "samples": len(picked),
+            "period_ms": 1000.0 * self.period_s,
+            "window_ms": None if self.window is None or self.window[1] is None
+            else 1000.0 * (self.window[1] - self.window[0]),
+            "source": "nvml" if self._smi is None else "nvidia-smi",
         }
 
 
@@ -246,19 +312,29 @@ def make_operands_on_device(m, n_local, k, n0, device, dist="square"):
     return a, sfa, b, sfb
 
 
-def run_cpu_baseline(a, sfa, b, sfb, m, n, k, budget_rows=4096):
-    """Time the contract's CPU path on an (Ms x Ns x K) sample of the resident operands."""
+CPU_SAMPLE_ROWS = 4096  # rows of A and of B in the CPU legs' sub-GEMM (K as the workload)
 
-    import numpy as np
-    import torch
 
-    from oracle.cpu_contract import time_cpu_contract, unswizzle_rows
+def cpu_sample(m, n, k, dist):
+    """The CPU legs' operands: a seeded CPU_SAMPLE_ROWS x CPU_SAMPLE_ROWS x K sample of the workload."""
 
-    ms, ns = min(budget_rows, m), min(budget_rows, b.shape[0])
-    a_s = a[:ms].cpu()
-    b_s = b[:ns].cpu()
-    sfa_s = unswizzle_rows(sfa.cpu(), np.arange(ms), k)
-    sfb_s = unswizzle_rows(sfb.cpu(), np.arange(ns), k)
+    from oracle.cpu_contract import cpu_sample_operands
+
+    ms, ns = min(CPU_SAMPLE_ROWS, m), min(CPU_SAMPLE_ROWS, n)
+    return (ms, ns) + tuple(cpu_sample_operands(ms, ns, k, dist=dist, seed=SEED))
+
+
+def cpu_sample_text(ms, ns, m, n, k, dist, how):
+    return (f"{ms}x{ns}x{k} sub-GEMM of the {m}x{n}x{k} workload ({dist} generator, seed {SEED}, OCP MX "
+            f"quantised on the CPU): torch CPU dequant + fp32 matmul + bf16 cast, {how}")
+
+
+def run_cpu_baseline(m, n, k, dist):
+    """Time the contract's CPU path on the same seeded sample ``--impl reference`` times."""
+
+    from oracle.cpu_contract import time_cpu_contract
+
+    ms, ns, a_s, sfa_s, b_s, sfb_s = cpu_sample(m, n, k, dist)
     secs, threads, reps = time_cpu_contract(a_s, sfa_s, b_s, sfb_s)
     flops = 2.0 * ms * ns * k
     return {
@@ -266,18 +342,16 @@ def run_cpu_baseline(a, sfa, b, sfb, m, n, k, budget_rows=4096):
         "unit": "TFLOP/s",
         "cores": threads,
         "kind": "port",
-        "sample": f"{ms}x{ns}x{k} sub-GEMM (first rows of A and B) of the {m}x{n}x{k} workload, "
-                  f"torch CPU dequant+fp32 matmul+bf16 cast, median of {reps} runs, {secs:.3f} s each",
+        "sample": cpu_sample_text(ms, ns, m, n, k, dist, f"median of {reps} runs of {secs:.3f} s"),
     }
 
 
 def bench_reference(args):
-    """--impl reference: the CPU contract path on bounded samples (rank 0 only)."""
+    """--impl reference: the contract's CPU path on the host cores (rank 0 only), same sample as cpu_baseline."""
 
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    import numpy as np
     import torch
 
     from oracle.cpu_contract import cpu_contract_gemm
@@ -285,13 +359,7 @@ def bench_reference(args):
     m, n, k = args.m, args.n, args.k
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    ms, ns = min(2048, m), min(2048, n)
-    g = torch.Generator().manual_seed(SEED)
-    a = torch.randint(0, 0x7E, (ms, k), dtype=torch.uint8, generator=g)
-    b = torch.randint(0, 0x7E, (ns, k), dtype=torch.uint8, generator=g)
-    a[:, ::2] |= 0x80
-    sfa = torch.randint(110, 130, (ms, k // 32), dtype=torch.uint8, generator=g)
-    sfb = torch.randint(110, 130, (ns, k // 32), dtype=torch.uint8, generator=g)
+    ms, ns, a, sfa, b, sfb = cpu_sample(m, n, k, args.dist)
     for _ in range(max(1, args.warmup)):
         cpu_contract_gemm(a, sfa, b, sfb)
     times = []
@@ -302,8 +370,7 @@ def bench_reference(args):
     total = sum(times)
     flops = 2.0 * ms * ns * k
     value = flops * len(times) / total / 1e12
-    sample = (f"{ms}x{ns}x{k} sub-GEMM per step of the {m}x{n}x{k} workload (random E4M3 codes, "
-              f"E8M0 scales 2^-17..2^2), torch CPU dequant + fp32 matmul + bf16 cast")
+    sample = cpu_sample_text(ms, ns, m, n, k, args.dist, f"{len(times)} timed steps, {threads} threads")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -318,7 +385,7 @@ def bench_reference(args):
         "vs_baseline": None,
         "dtype": "e4m3xe4m3->f32->bf16",
         "data": "synthetic",
-        "config": {"workload": workload_name(m, n, k), "m": m, "n": n, "k": k, "sample_m": ms, "sample_n": ns},
+        "config": workload_config(m, n, k, world, args.dist),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
@@ -375,14 +442,14 @@ def bench_cutex(args):
             graph.replay()  # first replay outside the timed region
         torch.cuda.synchronize()
 
-    sampler = ClockSampler(physical_gpu_index(local))
-    sampler.start()
-    time.sleep(0.5)
+    sampler = ClockSampler(physical_gpu_index(local)).start()
+    time.sleep(0.1)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    sampler.mark()
     with torch.cuda.stream(stream):
         start.record(stream)
         if graph is not None:
@@ -392,6 +459,7 @@ def bench_cutex(args):
                 step()
         end.record(stream)
     torch.cuda.synchronize()
+    sampler.close()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
@@ -403,10 +471,10 @@ def bench_cutex(args):
     # (power-capped steady state on a 1 kW part), reported beside the timed value.
     sustained = None
     if args.sustained_s > 0:
-        sampler2 = ClockSampler(physical_gpu_index(local))
-        sampler2.start()
+        sampler2 = ClockSampler(physical_gpu_index(local), period_s=0.05).start()
         s4, e4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         launches = 0
+        sampler2.mark()
         t_wall = time.time()
         with torch.cuda.stream(stream):
             s4.record(stream)
@@ -420,12 +488,19 @@ def bench_cutex(args):
                 stream.synchronize()
             e4.record(stream)
         torch.cuda.synchronize()
+        sampler2.close()
         clocks2 = sampler2.stop()
         ts = torch.tensor([s4.elapsed_time(e4)], dtype=torch.float64, device=device)
         if world > 1:
             dist.all_reduce(ts, op=dist.ReduceOp.MAX)
-        sustained = {"value": 2.0 * m * n * k * launches / (float(ts[0]) / 1e3) / 1e12, "unit": "TFLOP/s",
-                     "launches": launches, "seconds": float(ts[0]) / 1e3, "clocks": clocks2}
+        sustained_value = 2.0 * m * n * k * launches / (float(ts[0]) / 1e3) / 1e12
+        peak_s, peak_s_src = fp8_peak(load_peaks()[0], load_peaks()[1], True)
+        sustained = {"value": sustained_value, "unit": "TFLOP/s", "launches": launches,
+                     "seconds": float(ts[0]) / 1e3, "clocks": clocks2,
+                     "frac": sustained_value / world / peak_s, "peak": peak_s, "peak_source": peak_s_src}
+        if clocks2.get("power_w_median"):
+            # Energy per GEMM at the power cap: median board power x time per launch (per GPU).
+            sustained["joules_per_gemm"] = clocks2["power_w_median"] * float(ts[0]) / launches
     # Back-to-back launches in one graph: the average launch duration is the
     # timed interval over the launch count (inter-kernel gaps included).
     t = torch.tensor([elapsed_ms, elapsed_ms / args.steps], dtype=torch.float64, device=device)
@@ -562,7 +637,6 @@ def bench_cutex(args):
         allgather = {"nccl_ms": float(tg[0]), "gemm_ms": launch_avg_ms,
                      "gemm_then_nccl_ms": launch_avg_ms + float(tg[0]),
                      "bytes_per_rank_received": int(full.numel() * 2 * (world - 1) / world)}
-        del full
         # The same result with the gather fused into the GEMM's epilogue (peer TMA
         # stores over NVLink) and a one-element all-reduce as the closing barrier.
         from cutex_b200.sharding import FusedAllGatherGemm
@@ -572,6 +646,12 @@ def bench_cutex(args):
             for _ in range(2):
                 fused(a, b, sfa, sfb, stream=stream)
         torch.cuda.synchronize()
+        # Every rank's gathered D from the fused path equals the NCCL-gathered one, bit for bit.
+        same = torch.tensor([1.0 if torch.equal(fused.d_full.view(torch.int16), full.view(torch.int16)) else 0.0],
+                            dtype=torch.float64, device=device)
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        allgather["bitwise_ok"] = bool(same[0] == 1.0)
+        del full
         dist.barrier()
         s5, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 5
@@ -594,9 +674,15 @@ def bench_cutex(args):
     if args.vs_cublaslt > 0 and world == 1:
         cublaslt = compare_cublaslt(args, a, sfa, b, sfb, d, graph, step, stream, m, n, k)
 
+    side = None
+    if world == 1 and not args.no_configs:
+        del graph
+        graph = None
+        side = bench_configs(args, device, stream)
+
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_baseline = run_cpu_baseline(a, sfa, b, sfb, m, n, k)
+        cpu_baseline = run_cpu_baseline(m, n, k, args.dist)
 
     if rank == 0:
         traffic = recorded_traffic(workload, world)
@@ -613,17 +699,8 @@ def bench_cutex(args):
             "vs_baseline": None,
             "dtype": "e4m3xe4m3->f32->bf16",
             "data": "synthetic",
-            "config": {
-                "workload": workload,
-                "m": m, "n": n, "k": k,
-                "parallelism": f"n-shard{world}" if world > 1 else "single",
-                "n_per_gpu": n_local,
-                "kernel": plan,
-                "l2": "no flush: operands (E4M3 A + B slice + scales) exceed the 126 MB L2",
-                "inputs": ("N(0,1) x per-row 2^U(-4,4)" if args.dist == "square" else
-                           "activations N(0,1) with 0.1% of channels x50, weights N(0,0.02)")
-                          + ", quantised on the GPU (OCP MX, seed 0)",
-            },
+            "config": workload_config(m, n, k, world, args.dist),
+            "kernel_plan": dict(plan, n_per_gpu=n_local),
             "roofline": {
                 "bound": "hbm" if hbm_bound else "tensor",
                 "achieved": achieved,
@@ -647,6 +724,14 @@ def bench_cutex(args):
             line["allgather"] = allgather
         if cublaslt is not None:
             line["cublaslt"] = cublaslt
+            if "value" in cublaslt:
+                # This kernel over cuBLASLt's MXFP8 GEMM on the same operands, alternating graph
+                # replays in the same run (a comparator, not a roofline).
+                line["vs_cublaslt"] = {"ratio": cublaslt["cutex_value_same_rounds"] / cublaslt["value"],
+                                       "cublaslt_tflops": cublaslt["value"],
+                                       "bitwise_equal": cublaslt["bitwise_equal"]}
+        if side is not None:
+            line["configs"] = side
         print(json.dumps(line), flush=True)
 
     del graph
@@ -703,13 +788,13 @@ def compare_cublaslt(args, a, sfa, b, sfb, d, graph, step, stream, m, n, k):
         mine.append(timed(ours))
         theirs.append(timed(lt_graph.replay))
     sustained = None
-    if args.sustained_s > 0:
+    if args.sustained_s > 0 and args.cublaslt_sustained:
         # The same back-to-back protocol as this kernel's `sustained` entry.
         time.sleep(1.0)
-        sampler = ClockSampler(physical_gpu_index(0))
-        sampler.start()
+        sampler = ClockSampler(physical_gpu_index(0), period_s=0.05).start()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         launches = 0
+        sampler.mark()
         t_wall = time.time()
         with torch.cuda.stream(stream):
             s2.record(stream)
@@ -719,6 +804,7 @@ def compare_cublaslt(args, a, sfa, b, sfb, d, graph, step, stream, m, n, k):
                 stream.synchronize()
             e2.record(stream)
         torch.cuda.synchronize()
+        sampler.close()
         secs = s2.elapsed_time(e2) / 1e3
         sustained = {"value": 2.0 * m * n * k * launches / secs / 1e12, "unit": "TFLOP/s", "launches": launches,
                      "seconds": secs, "clocks": sampler.stop()}
@@ -731,29 +817,22 @@ def compare_cublaslt(args, a, sfa, b, sfb, d, graph, step, stream, m, n, k):
             "path": "torch._scaled_mm (cuBLASLt MXFP8, E4M3 x E4M3, E8M0 1x32 scales -> BF16), CUDA graph"}
 
 
-def bench_quantize(args):
-    """The MXFP8 quantisers (the step before the GEMM) on an [M, K] input, device-timed.
+def time_quantizer(kind, qdtype, m, k, steps, warmup, dev, stream):
+    """Device time per launch of one MXFP8 quantiser on a seeded [m, k] input (one CUDA graph of ``steps``).
 
-    Rowwise: x [M, K] -> E4M3 [M, K] + 1x32 E8M0 scales along K (128x4 layout).
-    Columnwise: x [M, K] -> E4M3 [K, M] = quantise(x^T) + scales of a [K, M]
-    operand. Algorithmic bytes per launch: M*K*(input bytes + 1) + M*K/32; one CUDA
-    graph of `steps` launches; the 1 GB (f32) or 512 MB (bf16) input exceeds the L2."""
+    Returns (ms per launch, algorithmic bytes per launch, clocks of the timed window)."""
     import torch
 
     from cutex_b200.kernels import quantize_mxfp8, quantize_mxfp8_columnwise
     from cutex_b200.kernels.dense_gemm import scale_buffer_bytes
 
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
-    m, k = args.m, args.k
     g = torch.Generator(device=dev).manual_seed(SEED)
     x = torch.randn(m, k, device=dev, generator=g)
     x *= torch.exp2(torch.empty(m, 1, device=dev).uniform_(-4.0, 4.0, generator=g))
-    if args.qdtype == "bf16":
+    if qdtype == "bf16":
         x = x.to(torch.bfloat16)
-    stream = torch.cuda.Stream(dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
-    if args.quantize == "rowwise":
+    if kind == "rowwise":
         q = torch.empty(m, k, dtype=torch.uint8, device=dev)
         sf = torch.empty(scale_buffer_bytes(m, k), dtype=torch.uint8, device=dev)
         step = lambda: quantize_mxfp8(x, q=q, sf=sf, stream=stream)  # noqa: E731
@@ -763,30 +842,49 @@ def bench_quantize(args):
         step = lambda: quantize_mxfp8_columnwise(x, qt=q, sft=sf, stream=stream)  # noqa: E731
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
+        for _ in range(max(warmup, 3)):
             step()
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         graph.replay()
     torch.cuda.synchronize()
-    sampler = ClockSampler(physical_gpu_index(0))
-    sampler.start()
-    time.sleep(0.3)
+    sampler = ClockSampler(physical_gpu_index(dev.index or 0)).start()
+    time.sleep(0.1)
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.mark()
     with torch.cuda.stream(stream):
         s0.record(stream)
         graph.replay()
         s1.record(stream)
     torch.cuda.synchronize()
+    sampler.close()
     clocks = sampler.stop()
-    ms = s0.elapsed_time(s1) / args.steps
-    in_bytes = 4 if args.qdtype == "f32" else 2
+    ms = s0.elapsed_time(s1) / steps
+    in_bytes = 4 if qdtype == "f32" else 2
     nbytes = float(m * k * (in_bytes + 1) + m * k // 32)
+    del graph
+    return ms, nbytes, clocks
+
+
+def bench_quantize(args):
+    """The MXFP8 quantisers (the step before the GEMM) on an [M, K] input, device-timed.
+
+    Rowwise: x [M, K] -> E4M3 [M, K] + 1x32 E8M0 scales along K (128x4 layout).
+    Columnwise: x [M, K] -> E4M3 [K, M] = quantise(x^T) + scales of a [K, M]
+    operand. Algorithmic bytes per launch: M*K*(input bytes + 1) + M*K/32; one CUDA
+    graph of `steps` launches; the 1 GB (f32) or 512 MB (bf16) input exceeds the L2."""
+    import torch
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    m, k = args.m, args.k
+    stream = torch.cuda.Stream(dev)
+    ms, nbytes, clocks = time_quantizer(args.quantize, args.qdtype, m, k, args.steps, args.warmup, dev, stream)
     peaks, source = load_peaks()
     achieved = nbytes / (ms / 1e3) / 1e9
     peak = float(peaks["hbm_gbs"])
@@ -801,7 +899,111 @@ def bench_quantize(args):
                      "algorithmic_bytes_per_launch": nbytes, "launch_avg_ms": ms},
         "gpu_launches": args.steps, "clocks": clocks,
     }), flush=True)
-    del graph
+
+
+# Other BASELINE configurations timed beside the headline in the default N = 1 run:
+# (name, M, N, K, input distribution, launches per timed region, L2 policy).
+SIDE_GEMMS = (
+    ("mxfp8_fprop_m4096_n4096_k4096", 4096, 4096, 4096, "square", 50, "flush"),
+    ("mxfp8_fprop_m8192_n28672_k8192", 8192, 28672, 8192, "llm", 20, "graph"),
+    ("mxfp8_fprop_m128_n28672_k8192", 128, 28672, 8192, "llm", 200, "graph"),
+    ("mxfp8_fprop_m16_n28672_k8192", 16, 28672, 8192, "llm", 200, "graph"),
+)
+SIDE_QUANTIZERS = (("rowwise", "f32"), ("rowwise", "bf16"), ("columnwise", "bf16"))
+
+
+def roofline_entry(flops, nbytes, ms, peaks, source):
+    """Both rates of one launch and the fraction of the roofline that bounds its shape."""
+
+    hbm_bound = flops / nbytes < RIDGE_FLOP_PER_BYTE
+    tflops = flops / (ms / 1e3) / 1e12
+    gbs = nbytes / (ms / 1e3) / 1e9
+    if hbm_bound:
+        peak, unit, achieved, src = float(peaks["hbm_gbs"]), "GB/s", gbs, f"{source} HBM copy (hbm_gbs)"
+    else:
+        peak, src = fp8_peak(peaks, source, False)
+        unit, achieved = "TFLOP/s", tflops
+    return {"tflops": tflops, "gbs": gbs,
+            "roofline": {"bound": "hbm" if hbm_bound else "tensor", "achieved": achieved, "peak": peak, "unit": unit,
+                         "frac": achieved / peak, "peak_source": src}}
+
+
+def bench_configs(args, dev, stream):
+    """BASELINE's other configurations, each timed on the device in this run (N = 1).
+
+    GEMMs whose operands exceed the 126 MB L2 are timed as one CUDA graph of
+    back-to-back launches; 4096^3 (operands and D fit in L2) is timed launch by
+    launch with a 256 MB L2 flush before each (``cuda_benchmark(flush_l2=True)``,
+    median). Each entry carries its clocks, kernel plan and roofline fraction."""
+    import torch
+
+    from cutex_b200 import _lib
+    from cutex_b200.benchmark import cuda_benchmark
+    from cutex_b200.kernels import PreparedGemm, query
+
+    peaks, source = load_peaks()
+    out = {}
+    for name, m, n, k, dist, reps, policy in SIDE_GEMMS:
+        a, sfa, b, sfb = make_operands_on_device(m, n, k, 0, dev, dist)
+        d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            step = PreparedGemm(a, b, sfa, sfb, d, stream=stream)
+            for _ in range(5):
+                step()
+        torch.cuda.synchronize()
+        sampler = ClockSampler(physical_gpu_index(dev.index or 0)).start()
+        if policy == "graph":
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(reps):
+                    step()
+            with torch.cuda.stream(stream):
+                graph.replay()
+            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            sampler.mark()
+            with torch.cuda.stream(stream):
+                s0.record(stream)
+                graph.replay()
+                s1.record(stream)
+            torch.cuda.synchronize()
+            sampler.close()
+            ms = s0.elapsed_time(s1) / reps
+            l2 = "no flush: B exceeds the 126 MB L2; one CUDA graph of back-to-back launches"
+            del graph
+        else:
+            sampler.mark()
+            with torch.cuda.stream(stream):
+                st = cuda_benchmark(step, warmup=3, rep=reps, stream=stream, flush_l2=True)
+            torch.cuda.synchronize()
+            sampler.close()
+            ms = st.median_us / 1e3
+            l2 = "256 MB L2 flush before every launch (outside its event pair); median of per-launch events"
+        if _lib.load().cutex_last_device_status(stream.cuda_stream) != 0:
+            raise RuntimeError(f"device-side timeout in {name}")
+        flops = 2.0 * m * n * k
+        nbytes = float(m * k + n * k + (m + n) * (k // 32) + 2 * m * n)
+        plan = query(m, n, k)
+        entry = {"m": m, "n": n, "k": k, "inputs": dist, "launches": reps, "ms_per_launch": ms,
+                 "kernel": {key: plan[key] for key in ("kernel", "tile_m", "tile_n", "stages", "grid_ctas",
+                                                       "split_k", "scheduler")},
+                 "l2": l2, "clocks": sampler.stop()}
+        entry.update(roofline_entry(flops, nbytes, ms, peaks, source))
+        out[name] = entry
+        del a, sfa, b, sfb, d, step
+        torch.cuda.empty_cache()
+    for kind, qdtype in SIDE_QUANTIZERS:
+        m = k = 16384
+        ms, nbytes, clocks = time_quantizer(kind, qdtype, m, k, 20, 3, dev, stream)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[f"mxfp8_quantize_{kind}_{qdtype}_m{m}_k{k}"] = {
+            "m": m, "k": k, "launches": 20, "ms_per_launch": ms, "gbs": gbs, "clocks": clocks,
+            "l2": "no flush: the input exceeds the 126 MB L2; one CUDA graph of back-to-back launches",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                         "frac": gbs / float(peaks["hbm_gbs"]), "peak_source": f"{source} HBM copy (hbm_gbs)"}}
+        torch.cuda.empty_cache()
+    return out
 
 
 def measure_fp8_peak(args):
@@ -832,10 +1034,10 @@ def measure_fp8_peak(args):
         e.record()
         e.synchronize()
         best = min(best, s.elapsed_time(e))
-    sampler = ClockSampler(physical_gpu_index(0))
-    sampler.start()
+    sampler = ClockSampler(physical_gpu_index(0), period_s=0.05).start()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     count = 0
+    sampler.mark()
     t0 = time.time()
     s.record()
     while time.time() - t0 < 4.0:
@@ -845,6 +1047,7 @@ def measure_fp8_peak(args):
         torch.cuda.synchronize()
     e.record()
     e.synchronize()
+    sampler.close()
     clocks = sampler.stop()
     out = {
         "tflops": flops / best / 1e9,

@@ -6,6 +6,7 @@ includes every kernel of the library) with nvcc into ``cutex_b200/_lib``.
 
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -42,18 +43,39 @@ def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE_DIR.glob("*.h"))
 
 
-def is_stale() -> bool:
-    if not LIB_PATH.exists():
+STAMP_PATH = LIB_DIR / (LIB_NAME + ".sha256")
+
+
+def source_digest(extra_flags: list[str] | None = None) -> str:
+    """SHA-256 over every source file's name and bytes and the compiler flags.
+
+    The library is rebuilt when this differs from the digest recorded beside it
+    at its last build, so a copied or checked-out tree whose file times say
+    nothing (the built library travels with the sources) still rebuilds exactly
+    when a source or a flag changed."""
+
+    h = hashlib.sha256()
+    for flag in [*NVCC_FLAGS, *(extra_flags or [])]:
+        h.update(flag.encode() + b"\0")
+    for src in sources():
+        h.update(src.name.encode() + b"\0")
+        h.update(src.read_bytes())
+        h.update(b"\0")
+    return h.hexdigest()
+
+
+def is_stale(extra_flags: list[str] | None = None) -> bool:
+    if not LIB_PATH.exists() or not STAMP_PATH.exists():
         return True
-    built = LIB_PATH.stat().st_mtime
-    return any(src.stat().st_mtime > built for src in sources())
+    return STAMP_PATH.read_text().strip() != source_digest(extra_flags)
 
 
 def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
-    """Compile the shared library if it is missing or older than its sources."""
+    """Compile the shared library if it is missing or its sources or flags changed since it was built."""
 
-    if not force and not is_stale():
+    if not force and not is_stale(extra_flags):
         return LIB_PATH
+    digest = source_digest(extra_flags)
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     tmp = LIB_DIR / f".{LIB_NAME}.{os.getpid()}.tmp"
     cmd = [_nvcc(), *NVCC_FLAGS, *(extra_flags or []), "-o", str(tmp), str(CSRC / "cutex_abi.cu")]
@@ -63,6 +85,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{proc.stderr[-8000:]}")
     os.replace(tmp, LIB_PATH)
+    STAMP_PATH.write_text(digest + "\n")
     return LIB_PATH
 
 

@@ -1,41 +1,58 @@
-"""Configuration binding plus persistent first-use autotuning.
+"""``cutex_b200.compile``: pick a native GEMM configuration on first use and remember it.
 
-Same contract as the reference's ``cutex.compile`` (``cutex/compiler.py:189-306``):
+Public surface (kept so code written against the reference's ``cutex.compile``,
+``cutex/compiler.py:189-306``, keeps working): ``compile(kernel, *args,
+verbose=, force_retune=, cache_path=, do_bench=, **kwargs)`` returning a
+``CompiledKernel``, ``AutotuneError`` when no candidate survives, and the cache
+file format version 1::
 
-* a launcher without an ``@autotune`` spec is bound once and returned;
-* with a spec, the key fields are read from the call's arguments, the JSON
-  cache (format version 1: ``{"version": 1, "entries": [{"kernel", "key",
-  "best_config": {"name", "kwargs"}, "candidate_timings_us"}]}``) is consulted
-  and, on a miss or ``force_retune``, every candidate is bound and timed
-  (median of CUDA-event samples); failing candidates are skipped, the fastest
-  is persisted atomically (temp file + ``os.replace``);
-* ``do_bench(compiled, *runtime_args, warmup=, rep=, **runtime_kwargs)``
-  returns microseconds; ``_compile_fn`` is the injection point tests use.
+    {"version": 1, "entries": [{"kernel": "<module>.<qualname>",
+                                "key": {<key field>: <value>, ...},
+                                "best_config": {"name": ..., "kwargs": {...}},
+                                "candidate_timings_us": {<label>: <us>, ...}}]}
 
-The kernels are compiled ahead of time (``libcutex_mxfp8.so``), so "compile"
-here binds the candidate's native config fields to the launcher; nothing is
-JIT-compiled at run time.
+so a cache written by either implementation is read by the other.
+
+How it works here. The kernels are compiled ahead of time into
+``libcutex_mxfp8.so``; a candidate is a set of ``cutex_gemm_config`` fields, and
+"compiling" it means binding those fields to the launcher (``bind_config``).
+A request goes through three steps:
+
+1. ``_request_key``: the autotune key fields are looked up by name among the
+   call's arguments (``mxfp8_gemm_launch`` keys on M, N, K and a device target
+   string that carries the GPU name, compute capability, SM count and
+   ``cutex_version()``, so a cache never crosses devices or library builds);
+2. ``TuneCache.lookup``: a stored choice for (launcher, key) is used only if it
+   is still one of the launcher's candidates;
+3. ``_Search.run``: otherwise every candidate is bound, timed with CUDA events
+   (``cutex_b200.benchmark.cuda_benchmark``, median) and then checked with the
+   launcher's device health probe, if it has one (attribute
+   ``__cutex_device_status__``: a callable returning the library's
+   ``cutex_last_device_status`` for the stream). A candidate that raised or left
+   a non-zero device status (a bounded wait that expired, a device-side check)
+   is rejected; the fastest remaining one is stored and returned.
 """
 
 from __future__ import annotations
 
-import functools
 import inspect
 import json
 import os
-from dataclasses import dataclass
+import tempfile
+from dataclasses import dataclass, field
 from pathlib import Path
-from typing import Any, Callable
+from typing import Any, Callable, Mapping
 
 from .autotune import AutotuneError, AutotuneSpec, Config, read_autotune_spec
 from .benchmark import cuda_benchmark
 
 CACHE_FORMAT_VERSION = 1
+DEVICE_STATUS_ATTRIBUTE = "__cutex_device_status__"
 
 
 @dataclass
 class CompiledKernel:
-    """The selected configuration bound to its launcher; calling it launches."""
+    """A launcher with its chosen configuration bound; calling it launches."""
 
     compiled: Callable[..., Any]
     best_config: Config
@@ -57,195 +74,218 @@ class CompiledKernel:
 
 
 def bind_config(kernel: Callable[..., Any], *args: Any, **kwargs: Any) -> Callable[..., Any]:
-    """Default "compile": fix the configuration keyword arguments of a launcher.
+    """Bind the configuration keywords ``kernel`` accepts; the result takes the call's arguments.
 
-    Positional ``args`` are only used for key resolution; the returned callable
-    takes the runtime arguments again, like a compiled CuTe function does.
+    ``args`` only serve key resolution and are not bound. Keywords the launcher
+    does not declare are dropped (a candidate may carry fields another launcher
+    of the same search space uses).
     """
 
-    sig = _signature(kernel)
-    config_kwargs = {k: v for k, v in kwargs.items() if k in sig.parameters}
-    return functools.partial(kernel, **config_kwargs)
+    accepted = _parameters(kernel)
+    fixed = {name: value for name, value in kwargs.items() if name in accepted}
+
+    def launch(*call_args: Any, **call_kwargs: Any):
+        return kernel(*call_args, **{**fixed, **call_kwargs})
+
+    launch.bound_config = dict(fixed)  # type: ignore[attr-defined]
+    return launch
 
 
-def _signature(kernel) -> inspect.Signature:
+def _parameters(kernel) -> Mapping[str, inspect.Parameter]:
+    target = kernel if callable(kernel) and not isinstance(kernel, type) else kernel.__call__
     try:
-        return inspect.signature(kernel)
+        return inspect.signature(target).parameters
     except (TypeError, ValueError):
-        return inspect.signature(kernel.__call__)
+        return inspect.signature(target.__call__).parameters
 
 
-def _json_value(value: Any) -> Any:
+def launcher_id(kernel) -> str:
+    """``module.qualname`` of the launcher: the cache's ``kernel`` field."""
+
+    for obj in (kernel, getattr(kernel, "__wrapped__", None), getattr(kernel, "fn", None)):
+        module = getattr(obj, "__module__", None)
+        name = getattr(obj, "__qualname__", None) or getattr(obj, "__name__", None)
+        if obj is not None and module and name:
+            return f"{module}.{name}"
+    return f"{type(kernel).__module__}.{type(kernel).__qualname__}"
+
+
+def _plain(value: Any) -> Any:
+    """A JSON-representable form of a key value (numbers, strings, lists, dicts; else its str)."""
+
     if value is None or isinstance(value, (bool, int, float, str)):
         return value
+    if isinstance(value, Mapping):
+        return {str(k): _plain(v) for k, v in value.items()}
     if isinstance(value, (list, tuple)):
-        return [_json_value(v) for v in value]
-    if isinstance(value, dict):
-        return {str(k): _json_value(v) for k, v in value.items()}
-    inner = getattr(value, "value", None)
-    if inner is not None and inner is not value:
-        return _json_value(inner)
+        return [_plain(v) for v in value]
+    item = getattr(value, "item", None)  # numpy / torch scalars
+    if callable(item) and getattr(value, "ndim", 1) == 0:
+        return _plain(item())
     return str(value)
 
 
-def _resolve_key_values(kernel, spec: AutotuneSpec, args, kwargs) -> dict[str, Any]:
-    sig = _signature(kernel)
-    try:
-        values = dict(sig.bind_partial(*args, **kwargs).arguments)
-    except TypeError:
-        values = dict(zip(sig.parameters, args))
-        values.update(kwargs)
-    for name in spec.key:
-        if name not in values:
-            available = ", ".join(sorted(values)) or "none"
-            raise AutotuneError(f"missing autotune key field {name!r}; available fields: {available}")
-    return {name: _json_value(values[name]) for name in spec.key}
+def _request_key(kernel, spec: AutotuneSpec, args: tuple, kwargs: dict) -> dict[str, Any]:
+    """Values of the spec's key fields, found by parameter name among the call's arguments."""
+
+    named: dict[str, Any] = {}
+    positional = [p.name for p in _parameters(kernel).values()
+                  if p.kind in (inspect.Parameter.POSITIONAL_ONLY, inspect.Parameter.POSITIONAL_OR_KEYWORD)]
+    named.update(zip(positional, args))
+    named.update(kwargs)
+    missing = [name for name in spec.key if name not in named]
+    if missing:
+        have = ", ".join(sorted(named)) or "none"
+        raise AutotuneError(f"missing autotune key field {missing[0]!r}; available fields: {have}")
+    return {name: _plain(named[name]) for name in spec.key}
 
 
-def _is_constexpr(annotation: Any) -> bool:
-    text = str(annotation)
-    return getattr(annotation, "__name__", None) == "Constexpr" or text.endswith(".Constexpr") or text.endswith(
-        "Constexpr'>"
-    )
+class TuneCache:
+    """The JSON cache file: one choice per (launcher id, key values).
+
+    A missing, unreadable or other-version file reads as empty and is replaced
+    on the next store; stores rewrite the whole file through a temporary file
+    in the same directory and an atomic rename, so a reader never sees half a
+    file.
+    """
+
+    def __init__(self, path: str | os.PathLike[str] | None):
+        self.path = None if path is None else Path(path)
+        self.entries: list[dict[str, Any]] = self._load()
+
+    def _load(self) -> list[dict[str, Any]]:
+        if self.path is None or not self.path.exists():
+            return []
+        try:
+            doc = json.loads(self.path.read_text(encoding="utf-8"))
+        except (OSError, UnicodeDecodeError, ValueError):
+            return []
+        if not isinstance(doc, dict) or doc.get("version") != CACHE_FORMAT_VERSION:
+            return []
+        found = doc.get("entries")
+        return [e for e in found if isinstance(e, dict)] if isinstance(found, list) else []
+
+    @staticmethod
+    def _is(entry: dict[str, Any], kernel_id: str, key: dict[str, Any]) -> bool:
+        return entry.get("kernel") == kernel_id and entry.get("key") == key
+
+    def lookup(self, kernel_id: str, key: dict[str, Any], candidates) -> tuple[Config, dict[str, float]] | None:
+        for entry in self.entries:
+            if not self._is(entry, kernel_id, key):
+                continue
+            chosen = entry.get("best_config") or {}
+            for cand in candidates:
+                if chosen.get("name") == cand.name and chosen.get("kwargs") == dict(cand.kwargs):
+                    raw = entry.get("candidate_timings_us") or {}
+                    return cand, {str(label): float(us) for label, us in raw.items()}
+        return None
+
+    def store(self, kernel_id: str, key: dict[str, Any], chosen: Config, timings_us: dict[str, float]) -> None:
+        if self.path is None:
+            return
+        self.entries = [e for e in self.entries if not self._is(e, kernel_id, key)]
+        self.entries.append({"kernel": kernel_id, "key": key,
+                             "best_config": {"name": chosen.name, "kwargs": dict(chosen.kwargs)},
+                             "candidate_timings_us": dict(timings_us)})
+        self.path.parent.mkdir(parents=True, exist_ok=True)
+        fd, tmp = tempfile.mkstemp(prefix=f".{self.path.name}.", dir=self.path.parent)
+        try:
+            with os.fdopen(fd, "w", encoding="utf-8") as fh:
+                json.dump({"version": CACHE_FORMAT_VERSION, "entries": self.entries}, fh, indent=2, sort_keys=True)
+            os.replace(tmp, self.path)
+        except BaseException:
+            Path(tmp).unlink(missing_ok=True)
+            raise
 
 
-def _runtime_arguments(kernel, args, kwargs):
-    """Drop parameters annotated as compile-time constants from a launch."""
+@dataclass
+class _Search:
+    """Time every candidate of one request; keep the survivors."""
 
-    params = list(_signature(kernel).parameters.values())
-    rt_args = tuple(v for i, v in enumerate(args) if i >= len(params) or not _is_constexpr(params[i].annotation))
-    by_name = {p.name: p for p in params}
-    rt_kwargs = {k: v for k, v in kwargs.items() if k not in by_name or not _is_constexpr(by_name[k].annotation)}
-    return rt_args, rt_kwargs
+    kernel: Any
+    spec: AutotuneSpec
+    bind: Callable[..., Any]
+    bench: Callable[..., float] | None
+    verbose: bool
+    timings_us: dict[str, float] = field(default_factory=dict)
+    rejected: dict[str, str] = field(default_factory=dict)
 
+    def _log(self, text: str) -> None:
+        if self.verbose:
+            print(f"[cutex_b200.compile] {text}")
 
-def _kernel_identifier(kernel) -> str:
-    for target in (kernel, getattr(kernel, "__wrapped__", None), getattr(kernel, "fn", None)):
-        if target is None:
-            continue
-        module = getattr(target, "__module__", None)
-        qualname = getattr(target, "__qualname__", None) or getattr(target, "__name__", None)
-        if module and qualname:
-            return f"{module}.{qualname}"
-    cls = type(kernel)
-    return f"{cls.__module__}.{cls.__qualname__}"
+    def _time(self, bound, args, kwargs) -> float:
+        if self.bench is not None:
+            return float(self.bench(bound, *args, warmup=self.spec.warmup, rep=self.spec.rep, **kwargs))
+        return cuda_benchmark(bound, *args, warmup=self.spec.warmup, rep=self.spec.rep, **kwargs).median_us
 
-
-def _read_cache(path: Path) -> list[dict[str, Any]]:
-    try:
-        payload = json.loads(path.read_text(encoding="utf-8"))
-    except (OSError, ValueError):
-        return []
-    if not isinstance(payload, dict) or payload.get("version") != CACHE_FORMAT_VERSION:
-        return []
-    entries = payload.get("entries")
-    return [e for e in entries if isinstance(e, dict)] if isinstance(entries, list) else []
-
-
-def _write_cache(path: Path, entries: list[dict[str, Any]]) -> None:
-    path.parent.mkdir(parents=True, exist_ok=True)
-    tmp = path.with_suffix(path.suffix + f".{os.getpid()}.tmp")
-    tmp.write_text(
-        json.dumps({"version": CACHE_FORMAT_VERSION, "entries": entries}, indent=2, sort_keys=True),
-        encoding="utf-8",
-    )
-    os.replace(tmp, path)
-
-
-def _matches(entry: dict[str, Any], kernel_id: str, key_values: dict[str, Any]) -> bool:
-    return entry.get("kernel") == kernel_id and entry.get("key") == key_values
-
-
-def _cached_choice(entries, kernel_id, key_values, configs):
-    for entry in entries:
-        if not _matches(entry, kernel_id, key_values):
-            continue
-        best = entry.get("best_config") or {}
-        for config in configs:
-            if best.get("name") == config.name and best.get("kwargs") == dict(config.kwargs):
-                timings = {str(k): float(v) for k, v in (entry.get("candidate_timings_us") or {}).items()}
-                return config, timings
-    return None
+    def run(self, args: tuple, kwargs: dict) -> tuple[Config, Callable[..., Any]]:
+        health = getattr(self.kernel, DEVICE_STATUS_ATTRIBUTE, None)
+        best: tuple[float, Config, Callable[..., Any]] | None = None
+        for cand in self.spec.configs:
+            try:
+                if cand.pre_hook is not None:
+                    cand.pre_hook(self.kernel, *args, **kwargs)
+                bound = self.bind(self.kernel, *args, **{**kwargs, **dict(cand.kwargs)})
+                us = self._time(bound, args, kwargs)
+                if not us >= 0.0:
+                    raise ValueError(f"benchmark returned {us!r}")
+                status = health() if health is not None else 0
+                if status:
+                    raise RuntimeError(f"device status {status} after the candidate ran")
+            except Exception as exc:  # the candidate is out; the search goes on
+                self.rejected[cand.label] = f"{type(exc).__name__}: {exc}"
+                self._log(f"rejected {cand.label}: {self.rejected[cand.label]}")
+                continue
+            self.timings_us[cand.label] = us
+            self._log(f"{cand.label}: {us:.3f} us")
+            if best is None or us < best[0]:  # ties keep the earlier candidate
+                best = (us, cand, bound)
+        if best is None:
+            lines = "\n".join(f"- {label}: {why}" for label, why in self.rejected.items())
+            raise AutotuneError(f"all autotune candidates failed\n{lines}")
+        self._log(f"selected {best[1].label}")
+        return best[1], best[2]
 
 
-def _persist(path, entries, kernel_id, key_values, config, timings_us) -> None:
-    kept = [e for e in entries if not _matches(e, kernel_id, key_values)]
-    kept.append(
-        {
-            "kernel": kernel_id,
-            "key": key_values,
-            "best_config": {"name": config.name, "kwargs": dict(config.kwargs)},
-            "candidate_timings_us": timings_us,
-        }
-    )
-    _write_cache(path, kept)
+def compile(kernel, *args: Any, verbose: bool = False, force_retune: bool | None = None,
+            cache_path: str | os.PathLike[str] | None = None, do_bench: Callable[..., float] | None = None,
+            _compile_fn: Callable[..., Any] | None = None, **kwargs: Any):
+    """Bind ``kernel``; if it carries an ``@autotune`` spec, choose (or recall) its fastest configuration.
 
+    ``args``/``kwargs`` are the launch's arguments: they supply the key fields and
+    are what each candidate is timed on. ``do_bench(bound, *args, warmup=, rep=,
+    **kwargs)`` replaces the CUDA-event timing (microseconds); ``_compile_fn``
+    replaces ``bind_config`` (tests inject fakes through both).
+    """
 
-def compile(
-    kernel,
-    *args: Any,
-    verbose: bool = False,
-    force_retune: bool | None = None,
-    cache_path: str | os.PathLike[str] | None = None,
-    do_bench: Callable[..., float] | None = None,
-    _compile_fn: Callable[..., Any] | None = None,
-    **kwargs: Any,
-):
-    """Bind ``kernel`` and, when it carries an autotune spec, pick and cache the fastest config."""
-
-    compile_fn = bind_config if _compile_fn is None else _compile_fn
+    bind = _compile_fn or bind_config
     spec = read_autotune_spec(kernel)
     if spec is None:
-        return compile_fn(kernel, *args, **kwargs)
+        return bind(kernel, *args, **kwargs)
 
-    force = spec.force_retune if force_retune is None else force_retune
-    path = Path(cache_path) if cache_path is not None else spec.cache_path
-    key_values = _resolve_key_values(kernel, spec, args, kwargs)
-    kernel_id = _kernel_identifier(kernel)
-    entries = _read_cache(path) if path is not None else []
+    key = _request_key(kernel, spec, args, kwargs)
+    kid = launcher_id(kernel)
+    cache = TuneCache(cache_path if cache_path is not None else spec.cache_path)
+    retune = spec.force_retune if force_retune is None else force_retune
 
-    hit = _cached_choice(entries, kernel_id, key_values, spec.configs) if spec.cache_results and not force else None
-    if hit is not None:
-        config, timings = hit
-        if verbose:
-            print(f"[cutex.autotune] disk cache hit: {config.label}")
-        if config.pre_hook is not None:
-            config.pre_hook(kernel, *args, **kwargs)
-        bound = compile_fn(kernel, *args, **{**kwargs, **dict(config.kwargs)})
-        return CompiledKernel(bound, config, timings, cache_hit="disk", cache_path=path)
-
-    rt_args, rt_kwargs = _runtime_arguments(kernel, args, kwargs)
-    bench = do_bench or spec.do_bench
-    failures: list[tuple[str, BaseException]] = []
-    measured: list[tuple[float, int, Config, Callable[..., Any]]] = []
-    timings_us: dict[str, float] = {}
-    for index, config in enumerate(spec.configs):
-        try:
-            if config.pre_hook is not None:
-                config.pre_hook(kernel, *args, **kwargs)
-            bound = compile_fn(kernel, *args, **{**kwargs, **dict(config.kwargs)})
-            if bench is None:
-                t = cuda_benchmark(bound, *rt_args, warmup=spec.warmup, rep=spec.rep, **rt_kwargs).median_us
-            else:
-                t = float(bench(bound, *rt_args, warmup=spec.warmup, rep=spec.rep, **rt_kwargs))
-            if t < 0:
-                raise ValueError("benchmark returned a negative duration")
-            timings_us[config.label] = t
-            measured.append((t, index, config, bound))
+    if spec.cache_results and not retune:
+        hit = cache.lookup(kid, key, spec.configs)
+        if hit is not None:
+            chosen, timings = hit
             if verbose:
-                print(f"[cutex.autotune] {config.label}: {t:.3f} us")
-        except Exception as exc:  # a failing candidate is recorded and skipped
-            failures.append((config.label, exc))
-            if verbose:
-                print(f"[cutex.autotune] rejected {config.label}: {type(exc).__name__}: {exc}")
+                print(f"[cutex_b200.compile] cache hit {cache.path}: {chosen.label}")
+            if chosen.pre_hook is not None:
+                chosen.pre_hook(kernel, *args, **kwargs)
+            bound = bind(kernel, *args, **{**kwargs, **dict(chosen.kwargs)})
+            return CompiledKernel(bound, chosen, timings, cache_hit="disk", cache_path=cache.path)
 
-    if not measured:
-        details = "\n".join(f"- {label}: {type(exc).__name__}: {exc}" for label, exc in failures)
-        raise AutotuneError(f"all autotune candidates failed\n{details}")
+    search = _Search(kernel, spec, bind, do_bench or spec.do_bench, verbose)
+    chosen, bound = search.run(args, kwargs)
+    if spec.cache_results:
+        cache.store(kid, key, chosen, search.timings_us)
+    return CompiledKernel(bound, chosen, dict(search.timings_us), cache_path=cache.path)
 
-    _, _, best, bound = min(measured, key=lambda item: (item[0], item[1]))
-    if verbose:
-        print(f"[cutex.autotune] selected: {best.label}")
-    if spec.cache_results and path is not None:
-        _persist(path, entries, kernel_id, key_values, best, timings_us)
-    return CompiledKernel(bound, best, timings_us, cache_path=path)
+
+__all__ = ["CACHE_FORMAT_VERSION", "CompiledKernel", "DEVICE_STATUS_ATTRIBUTE", "TuneCache", "bind_config",
+           "compile", "launcher_id"]

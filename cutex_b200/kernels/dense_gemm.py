@@ -27,6 +27,7 @@ from typing import Any
 
 from .. import _lib
 from ..autotune import Config, autotune
+from ..compiler import DEVICE_STATUS_ATTRIBUTE
 from .dense_gemm_contract import scale_buffer_bytes, validate_mxfp8_gemm_shape
 
 
@@ -325,6 +326,8 @@ GEMM_CONFIGS = (
                name=f"1cta_n128_s{s}_e{e}")
         for s, e in ((6, 1), (5, 2))
     ]
+    # M <= 128 only (larger M is rejected by the library and skipped by the search).
+    + [Config({"kernel": 3, "split_k": s}, name=f"skinny_split{s}") for s in (1, 2, 3)]
 )
 
 
@@ -337,6 +340,23 @@ def mxfp8_gemm_launch(a, b, sfa, sfb, out, m, n, k, target, stream=None, *, kern
     cfg = GemmConfig(kernel, tile_n, stages, raster_group, raster_along_n, split_k, max_ctas, epi_buffers,
                      sf_buffers, scheduler)
     return dense_gemm(a, b, sfa, sfb, out, stream=stream, config=cfg)
+
+
+def _launch_device_status() -> int:
+    """Health probe the autotuner runs after timing a candidate: the library's device status word.
+
+    Synchronises the device first (candidates may have run on any stream); a
+    non-zero value (an expired bounded wait, a device-side check) rejects the
+    candidate and clears the word.
+    """
+
+    import torch
+
+    torch.cuda.synchronize()
+    return int(_lib.load().cutex_last_device_status(torch.cuda.current_stream().cuda_stream))
+
+
+setattr(mxfp8_gemm_launch, DEVICE_STATUS_ATTRIBUTE, _launch_device_status)
 
 
 __all__ = [

@@ -65,14 +65,23 @@ def allgather_columns(d_local, world: int, group=None):
 class FusedAllGatherGemm:
     """N-sharded GEMM whose epilogue also writes each finished tile into every peer's full D.
 
-    Every rank holds a full ``d_full`` [M, N] (bf16). Rank r computes
-    ``d_full[:, n0:n1]`` from all of A and its B slice; the kernel stores each
-    finished chunk into its own copy and, over NVLink, into the same place of
-    every peer's copy (``cutex_mxfp8_gemm_allgather``), so the gather overlaps
-    the GEMM. The peer copies are mapped once with CUDA IPC (handles exchanged
-    through ``group``). A call ends with a one-element all-reduce on the
-    current stream; after it every rank's ``d_full`` is complete.
+    Every rank holds full [M, N] bf16 result buffers. Rank r computes its
+    columns ``[n0, n1)`` from all of A and its B slice; the kernel stores each
+    finished chunk into its own buffer and, over NVLink, into the same place of
+    every peer's buffer (``cutex_mxfp8_gemm_allgather``), so the gather overlaps
+    the GEMM. The peers' buffers are mapped once with CUDA IPC (handles
+    exchanged through ``group``). A call ends with a one-element all-reduce on
+    the call's stream; after it every rank's result is complete.
+
+    Two result buffers alternate between calls. Call k+1's peer stores go to
+    the other buffer, and call k+2's (into this buffer again) start only after
+    every rank has reached call k+1's closing all-reduce on its stream. So the
+    result of a call may be read by work enqueued on the stream before the next
+    call is made; work enqueued later may see it overwritten. ``d_full`` is the
+    buffer the last call wrote.
     """
+
+    BUFFERS = 2
 
     def __init__(self, m: int, n: int, k: int, group=None, config=None, device=None):
         import ctypes
@@ -91,32 +100,43 @@ class FusedAllGatherGemm:
         self.shard = shard_bounds(n, self.world, self.rank)
         self.m, self.n, self.k = m, n, k
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-        self.d_full = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
         lib = _lib.load()
-        handle = ctypes.create_string_buffer(64)
-        offset = ctypes.c_int64(0)
-        _lib.check(lib.cutex_ipc_export(self.d_full.data_ptr(), handle, ctypes.byref(offset)), "cutex_ipc_export")
-        entries = [None] * self.world
-        dist.all_gather_object(entries, (handle.raw, offset.value), group=group)
+        self._buffers = [torch.empty(m, n, dtype=torch.bfloat16, device=dev) for _ in range(self.BUFFERS)]
+        mine = []
+        for buf in self._buffers:
+            handle = ctypes.create_string_buffer(64)
+            offset = ctypes.c_int64(0)
+            _lib.check(lib.cutex_ipc_export(buf.data_ptr(), handle, ctypes.byref(offset)), "cutex_ipc_export")
+            mine.append((handle.raw, offset.value))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
         self._mappings = []
-        peers = []
-        for r, (h, off) in enumerate(entries):
-            if r == self.rank:
-                continue
-            ptr, mapping = ctypes.c_void_p(), ctypes.c_void_p()
-            _lib.check(lib.cutex_ipc_import(h, off, ctypes.byref(ptr), ctypes.byref(mapping)), "cutex_ipc_import")
-            self._mappings.append(mapping.value)
-            peers.append(ptr.value + self.shard.n0 * 2)  # this rank's columns in peer r's copy
-        self._peers = (ctypes.c_void_p * len(peers))(*peers)
-        self._maps = torch.empty(128 * len(peers), dtype=torch.uint8, device=dev)
-        # The peers' TMA store descriptors, written once (a host copy that waits
-        # for the stream would otherwise serialise every call).
-        _lib.check(lib.cutex_mxfp8_allgather_maps(self._peers, len(peers), m, self.shard.n, n, self._maps.data_ptr(),
-                                                  self._maps.numel(), torch.cuda.current_stream().cuda_stream),
-                   "cutex_mxfp8_allgather_maps")
+        self._maps = []
+        self.num_peers = self.world - 1
+        for i in range(self.BUFFERS):
+            peers = []
+            for r, exported in enumerate(everyone):
+                if r == self.rank:
+                    continue
+                h, off = exported[i]
+                ptr, mapping = ctypes.c_void_p(), ctypes.c_void_p()
+                _lib.check(lib.cutex_ipc_import(h, off, ctypes.byref(ptr), ctypes.byref(mapping)),
+                           "cutex_ipc_import")
+                self._mappings.append(mapping.value)
+                peers.append(ptr.value + self.shard.n0 * 2)  # this rank's columns in peer r's buffer i
+            ptrs = (ctypes.c_void_p * len(peers))(*peers)
+            maps = torch.empty(128 * len(peers), dtype=torch.uint8, device=dev)
+            # The peers' TMA store descriptors, written once (a host copy that waits
+            # for the stream would otherwise serialise every call).
+            _lib.check(lib.cutex_mxfp8_allgather_maps(ptrs, len(peers), m, self.shard.n, n, maps.data_ptr(),
+                                                      maps.numel(), torch.cuda.current_stream().cuda_stream),
+                       "cutex_mxfp8_allgather_maps")
+            self._maps.append(maps)
         torch.cuda.current_stream().synchronize()  # descriptors in place before any stream's GEMM reads them
         self._cfg = (config or GemmConfig()).to_c()
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        self._calls = 0
+        self.d_full = self._buffers[-1]
 
     def __call__(self, a, b_local, sfa, sfb_local, stream=None):
         import ctypes
@@ -125,19 +145,26 @@ class FusedAllGatherGemm:
         import torch.distributed as dist
 
         from . import _lib
-        from .kernels.dense_gemm import _stream_handle
 
-        handle = _stream_handle(stream)
+        if stream is None:
+            s = torch.cuda.current_stream()
+        elif isinstance(stream, int):
+            s = torch.cuda.ExternalStream(stream)
+        else:
+            s = stream
+        i = self._calls % self.BUFFERS
+        out = self._buffers[i]
         status = _lib.load().cutex_mxfp8_gemm_allgather(
             a.data_ptr(), b_local.data_ptr(), sfa.data_ptr(), sfb_local.data_ptr(),
-            self.d_full.data_ptr() + self.shard.n0 * 2, self.m, self.shard.n, self.k, self.n, self._maps.data_ptr(),
-            len(self._peers), ctypes.byref(self._cfg), handle)
+            out.data_ptr() + self.shard.n0 * 2, self.m, self.shard.n, self.k, self.n, self._maps[i].data_ptr(),
+            self.num_peers, ctypes.byref(self._cfg), s.cuda_stream)
         _lib.check(status, "cutex_mxfp8_gemm_allgather")
-        # Cross-rank barrier in stream order: every rank's pushes have landed.
-        s = stream if stream is not None and not isinstance(stream, int) else torch.cuda.current_stream()
+        self._calls += 1
+        self.d_full = out
+        # Cross-rank barrier in the call's stream order: every rank's pushes have landed.
         with torch.cuda.stream(s):
             dist.all_reduce(self._flag, group=self.group)
-        return self.d_full
+        return out
 
     def close(self) -> None:
         from . import _lib

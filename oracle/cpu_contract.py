@@ -53,3 +53,42 @@ def time_cpu_contract(a_codes, sfa_logical, b_codes, sfb_logical, *, min_seconds
         cpu_contract_gemm(a_codes, sfa_logical, b_codes, sfb_logical)
         times.append(time.perf_counter() - t0)
     return float(np.median(times)), threads, len(times)
+
+
+def cpu_sample_operands(rows_a: int, rows_b: int, K: int, dist: str = "square", seed: int = 0):
+    """Seeded MXFP8 operands on the CPU for timing the contract path: (a, sfa, b, sfb), logical scales.
+
+    Sources follow BASELINE's generators (``square``: N(0,1) x per-row
+    2^U(-4,4); ``llm``: activations N(0,1) with 0.1 % of K-channels x50, weights
+    N(0, 0.02)), drawn from a CPU ``torch.Generator``; quantisation is the OCP MX
+    rule of the oracle (scale byte = exponent field of the block amax - 8,
+    elements x * 2^(127 - byte) rounded to E4M3 with saturation), done with
+    torch's float8 cast so that a 4096-row sample takes about a second. Both
+    CPU timing legs of ``bench.py`` use this one function, so they time the same
+    operands.
+    """
+
+    g = torch.Generator().manual_seed(seed)
+
+    def source(rows, is_a):
+        x = torch.randn(rows, K, generator=g)
+        if dist == "llm":
+            if is_a:
+                x[:, torch.randperm(K, generator=g)[: max(1, K // 1000)]] *= 50.0
+            else:
+                x *= 0.02
+            return x
+        return x * torch.exp2(torch.empty(rows, 1).uniform_(-4.0, 4.0, generator=g))
+
+    def quantise(x):
+        rows = x.shape[0]
+        blocks = x.view(rows, K // 32, 32)
+        amax = blocks.abs().amax(dim=2)
+        sbyte = ((amax.view(torch.int32) >> 23) - 8).clamp(min=0)
+        mult = torch.ldexp(torch.ones(()), (127 - sbyte).float())
+        y = (blocks * mult.unsqueeze(-1)).clamp(-448.0, 448.0)
+        return y.to(torch.float8_e4m3fn).view(torch.uint8).view(rows, K), sbyte.to(torch.uint8)
+
+    a, sfa = quantise(source(rows_a, True))
+    b, sfb = quantise(source(rows_b, False))
+    return a, sfa, b, sfb

@@ -85,7 +85,9 @@ def encode_e4m3_rne_sat(y: np.ndarray) -> np.ndarray:
     # code m = round_half_even(a / 2^-9) maps 8 onto the first normal code 0x08.
     code[sub] = np.rint(a[sub] * 2.0**9).astype(np.int32)
 
-    nrm = ~sub
+    # Non-finite inputs never reach the exponent arithmetic: infinities saturate
+    # and NaN maps to 0x7F below.
+    nrm = ~sub & np.isfinite(a)
     an = a[nrm]
     e = np.floor(np.log2(an)).astype(np.int32)
     # Guard log2 rounding at exact powers of two.

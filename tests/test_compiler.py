@@ -148,3 +148,46 @@ def test_default_binding_fixes_config_kwargs():
 
     bound = bind_config(launcher, 1, 2, tile=128, stages=6, unrelated=5)
     assert bound(1, 2) == (1, 2, 128, 6)
+
+
+def test_candidate_leaving_a_device_error_is_rejected(tmp_path):
+    # The launcher's health probe reports a non-zero device status (e.g. an
+    # expired bounded wait) after the first candidate: that candidate is out
+    # even though it timed fastest.
+    from cutex_b200.compiler import DEVICE_STATUS_ATTRIBUTE
+
+    @autotune(configs=[Config({"tile": 1}, name="one"), Config({"tile": 2}, name="two")], key=["m"])
+    def kernel(m, tile=1):
+        return tile
+
+    statuses = iter([6, 0])
+    setattr(kernel, DEVICE_STATUS_ATTRIBUTE, lambda: next(statuses))
+    out = compile(kernel, 1, cache_path=tmp_path / "c.json", _compile_fn=lambda _k, *a, **kw: FakeCompiled(kw["tile"]),
+                  do_bench=lambda c, *a, **k: float(c.tile))
+    assert out.best_config.name == "two"
+    assert set(out.timings_us) == {"two"}
+    assert json.loads((tmp_path / "c.json").read_text())["entries"][0]["best_config"]["name"] == "two"
+
+
+def test_stale_cached_choice_outside_the_search_space_is_retuned(tmp_path):
+    @autotune(configs=[Config({"tile": 1}, name="one")], key=["m"])
+    def kernel(m, tile=1):
+        return tile
+
+    cache = tmp_path / "c.json"
+    from cutex_b200.compiler import launcher_id
+
+    cache.write_text(json.dumps({"version": 1, "entries": [{
+        "kernel": launcher_id(kernel), "key": {"m": 1}, "best_config": {"name": "gone", "kwargs": {"tile": 9}},
+        "candidate_timings_us": {"gone": 1.0}}]}))
+    out = compile(kernel, 1, cache_path=cache, _compile_fn=lambda _k, *a, **kw: FakeCompiled(kw["tile"]),
+                  do_bench=lambda *a, **k: 2.0)
+    assert out.cache_hit is None and out.best_config.name == "one"
+    assert [e["best_config"]["name"] for e in json.loads(cache.read_text())["entries"]] == ["one"]
+
+
+def test_gemm_launcher_carries_the_device_health_probe():
+    from cutex_b200.compiler import DEVICE_STATUS_ATTRIBUTE
+    from cutex_b200.kernels.dense_gemm import mxfp8_gemm_launch
+
+    assert callable(getattr(mxfp8_gemm_launch, DEVICE_STATUS_ATTRIBUTE))

@@ -165,3 +165,25 @@ def test_flops_and_bytes_per_baseline_table():
     assert O.dense_gemm_flops(16384, 16384, 16384) == 2 * 16384**3
     assert O.gemm_bytes(16384, 16384, 16384) == 1090519040  # 1090.5 MB
     assert O.gemm_bytes(16, 28672, 8192) == 243273728  # 243.3 MB
+
+
+def test_cpu_sample_operands_match_the_oracle_quantiser():
+    # The CPU timing legs' fast torch quantiser equals the oracle's on the same sources.
+    import torch
+
+    from oracle.cpu_contract import cpu_sample_operands
+
+    for dist in ("square", "llm"):
+        a, sfa, b, sfb = cpu_sample_operands(160, 96, 512, dist=dist, seed=3)
+        g = torch.Generator().manual_seed(3)
+        xa = torch.randn(160, 512, generator=g)
+        if dist == "llm":
+            xa[:, torch.randperm(512, generator=g)[:1]] *= 50.0
+            xb = torch.randn(96, 512, generator=g) * 0.02
+        else:
+            xa = xa * torch.exp2(torch.empty(160, 1).uniform_(-4.0, 4.0, generator=g))
+            xb = torch.randn(96, 512, generator=g)
+            xb = xb * torch.exp2(torch.empty(96, 1).uniform_(-4.0, 4.0, generator=g))
+        for (q, s), x in (((a, sfa), xa), ((b, sfb), xb)):
+            q_ref, s_ref = O.quantize_mxfp8(x.numpy())
+            assert np.array_equal(q.numpy(), q_ref) and np.array_equal(s.numpy(), s_ref)
