@@ -932,13 +932,14 @@ def bench_configs(args, dev, stream):
     """BASELINE's other configurations, each timed on the device in this run (N = 1).
 
     GEMMs whose operands exceed the 126 MB L2 are timed as one CUDA graph of
-    back-to-back launches; 4096^3 (operands and D fit in L2) is timed launch by
-    launch with a 256 MB L2 flush before each (``cuda_benchmark(flush_l2=True)``,
-    median). Each entry carries its clocks, kernel plan and roofline fraction."""
+    back-to-back launches; 4096^3 (operands and D fit in L2) with a 256 MB L2
+    flush before every launch, as the difference of two graphs (with and
+    without the GEMMs). Each entry carries its clocks, kernel plan and roofline
+    fraction."""
     import torch
 
     from cutex_b200 import _lib
-    from cutex_b200.benchmark import cuda_benchmark
+    from cutex_b200.benchmark import L2_FLUSH_BYTES
     from cutex_b200.kernels import PreparedGemm, query
 
     peaks, source = load_peaks()
@@ -973,13 +974,40 @@ def bench_configs(args, dev, stream):
             l2 = "no flush: B exceeds the 126 MB L2; one CUDA graph of back-to-back launches"
             del graph
         else:
-            sampler.mark()
+            # Operands and D fit in the L2: a 256 MB write flushes it before every launch.
+            # One graph of `reps` x (flush, GEMM) and one of `reps` x flush, each timed as a
+            # whole (so no host gap enters a timed interval); the GEMM's time is the
+            # difference, median of three alternating rounds.
+            flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+            g_both, g_flush = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_both, stream=stream):
+                for _ in range(reps):
+                    flush.zero_()
+                    step()
+            with torch.cuda.graph(g_flush, stream=stream):
+                for _ in range(reps):
+                    flush.zero_()
             with torch.cuda.stream(stream):
-                st = cuda_benchmark(step, warmup=3, rep=reps, stream=stream, flush_l2=True)
+                g_both.replay()
+                g_flush.replay()
             torch.cuda.synchronize()
+
+            def timed(g):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):
+                    e0.record(stream)
+                    g.replay()
+                    e1.record(stream)
+                torch.cuda.synchronize()
+                return e0.elapsed_time(e1)
+
+            sampler.mark()
+            diffs = sorted(timed(g_both) - timed(g_flush) for _ in range(3))
             sampler.close()
-            ms = st.median_us / 1e3
-            l2 = "256 MB L2 flush before every launch (outside its event pair); median of per-launch events"
+            ms = diffs[1] / reps
+            l2 = ("256 MB L2 flush before every launch: graph of (flush, GEMM) x launches minus graph of flush x "
+                  "launches, median of 3 rounds")
+            del g_both, g_flush, flush
         if _lib.load().cutex_last_device_status(stream.cuda_stream) != 0:
             raise RuntimeError(f"device-side timeout in {name}")
         flops = 2.0 * m * n * k

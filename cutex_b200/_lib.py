@@ -113,6 +113,7 @@ SIGNATURES = {
     "cutex_ipc_export": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_i64)]),
     "cutex_ipc_import": (ctypes.c_int, [_vp, _i64, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
     "cutex_ipc_close": (ctypes.c_int, [_vp]),
+    "cutex_mxfp8_selftest_wait_timeout": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "cutex_mxfp8_allgather_maps": (ctypes.c_int, [ctypes.POINTER(_vp), _i32, _i64, _i64, _i64, _vp, _i64, _vp]),
     "cutex_mxfp8_gemm_allgather": (
         ctypes.c_int,

@@ -73,12 +73,13 @@ class CompiledKernel:
         }
 
 
-def bind_config(kernel: Callable[..., Any], *args: Any, **kwargs: Any) -> Callable[..., Any]:
+def bind_config(kernel: Callable[..., Any], /, *args: Any, **kwargs: Any) -> Callable[..., Any]:
     """Bind the configuration keywords ``kernel`` accepts; the result takes the call's arguments.
 
     ``args`` only serve key resolution and are not bound. Keywords the launcher
     does not declare are dropped (a candidate may carry fields another launcher
-    of the same search space uses).
+    of the same search space uses). ``kernel`` is positional-only, so a launcher
+    may itself take a ``kernel`` keyword (the GEMM's kernel-family field).
     """
 
     accepted = _parameters(kernel)
@@ -248,7 +249,7 @@ class _Search:
         return best[1], best[2]
 
 
-def compile(kernel, *args: Any, verbose: bool = False, force_retune: bool | None = None,
+def compile(kernel, /, *args: Any, verbose: bool = False, force_retune: bool | None = None,
             cache_path: str | os.PathLike[str] | None = None, do_bench: Callable[..., float] | None = None,
             _compile_fn: Callable[..., Any] | None = None, **kwargs: Any):
     """Bind ``kernel``; if it carries an ``@autotune`` spec, choose (or recall) its fastest configuration.

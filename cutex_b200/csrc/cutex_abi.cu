@@ -197,13 +197,15 @@ struct Variant {
   const void* fn;
   const void* fn_trace;   // instrumented twin (cutex_mxfp8_gemm_trace), or null
   const void* fn_epi[4];  // fused-epilogue twins: [1] BF16 out, [2] E4M3 + scales out, [3] all-gather
+  const void* fn_fault;   // error-path self-test twin (cutex_mxfp8_selftest_wait_timeout), or null
   bool attr_set_trace[kMaxDevices];
+  bool attr_set_fault[kMaxDevices];
   bool attr_set[kMaxDevices];
   bool attr_set_epi[4][kMaxDevices];
   int max_clusters[kMaxDevices];
 };
 
-template <int CG, int BN, int S, int E, int F, bool D, bool T = false, bool X = false>
+template <int CG, int BN, int S, int E, int F, bool D, bool T = false, bool X = false, bool Q = false>
 Variant make_variant() {
   Variant v{};
   v.cta_group = CG;
@@ -219,6 +221,7 @@ Variant make_variant() {
   v.fn_epi[1] = X ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, false, 1>) : nullptr;
   v.fn_epi[2] = X ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, false, 2>) : nullptr;
   v.fn_epi[3] = X ? reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, false, 3>) : nullptr;
+  if constexpr (Q) v.fn_fault = reinterpret_cast<const void*>(&mxfp8_gemm_kernel<CG, BN, S, E, F, D, false, 0, true>);
   return v;
 }
 
@@ -233,7 +236,7 @@ Variant g_variants[] = {
     make_variant<1, 128, 6, 1, 1, true, false, true>(), make_variant<1, 128, 5, 2, 1, true>(),
     // static persistent scheduling
     make_variant<1, 128, 4, 2, 2, false>(), make_variant<1, 128, 5, 2, 2, false>(),
-    make_variant<1, 128, 6, 1, 2, false>(), make_variant<1, 128, 6, 1, 1, false>(),
+    make_variant<1, 128, 6, 1, 2, false>(), make_variant<1, 128, 6, 1, 1, false, false, false, true>(),
     make_variant<1, 256, 3, 2, 2, false>(), make_variant<1, 256, 4, 1, 2, false>(),
     make_variant<1, 256, 4, 1, 1, false, true>(), make_variant<2, 256, 4, 2, 2, false>(),
     make_variant<2, 256, 5, 2, 2, false>(), make_variant<2, 256, 6, 1, 2, false>(),
@@ -449,13 +452,16 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const void* sfa,
                 const void* sfb, void* d, int64_t M, int64_t N, int64_t K, int64_t ldd,
                 cudaStream_t stream, unsigned long long* trace = nullptr, int trace_cap = 0,
-                const cutex_epilogue* epi = nullptr, const CUtensorMap* peer_maps = nullptr, int num_peers = 0) {
+                const cutex_epilogue* epi = nullptr, const CUtensorMap* peer_maps = nullptr, int num_peers = 0,
+                int fault_kit = -1) {
   Variant* v = plan.variant;
   const bool traced = trace != nullptr;
+  const bool fault = fault_kit >= 0;
   if (traced && v->fn_trace == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
   const int epi_kind = peer_maps != nullptr ? 3 : (epi == nullptr ? 0 : (epi->out_dtype == 1 ? 2 : 1));
   if (epi_kind != 0 && (traced || v->fn_epi[epi_kind] == nullptr)) return CUTEX_ERR_INVALID_ARGUMENT;
-  const void* fn = traced ? v->fn_trace : (epi_kind != 0 ? v->fn_epi[epi_kind] : v->fn);
+  if (fault && (traced || epi_kind != 0 || v->fn_fault == nullptr)) return CUTEX_ERR_INVALID_ARGUMENT;
+  const void* fn = fault ? v->fn_fault : traced ? v->fn_trace : (epi_kind != 0 ? v->fn_epi[epi_kind] : v->fn);
   const int cg = v->cta_group;
   CUtensorMap ta, tb, tsa, tsb, td;
   const bool out_ok = epi_kind == 2 ? encode_output_fp8(&td, d, M, N, ldd) : encode_output(&td, d, M, N, ldd);
@@ -464,7 +470,9 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
     return CUTEX_ERR_CUDA;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    bool& set = traced ? v->attr_set_trace[dev] : (epi_kind != 0 ? v->attr_set_epi[epi_kind][dev] : v->attr_set[dev]);
+    bool& set = fault ? v->attr_set_fault[dev]
+                : traced ? v->attr_set_trace[dev]
+                         : (epi_kind != 0 ? v->attr_set_epi[epi_kind][dev] : v->attr_set[dev]);
     if (!set) {
       if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v->smem_bytes) !=
           cudaSuccess)
@@ -487,6 +495,7 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
   args.N = static_cast<int>(N);
   args.peer_maps = peer_maps;
   args.num_peers = num_peers;
+  args.fault_withhold_kit = fault_kit;
   if (epi != nullptr) {
     args.alpha = epi->alpha;
     args.beta = epi->beta;
@@ -842,6 +851,35 @@ extern "C" int cutex_mxfp8_gemm_trace(const void* a, const void* b, const void* 
   if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
   return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, ldd,
                      reinterpret_cast<cudaStream_t>(stream), trace, trace_cap);
+}
+
+extern "C" int cutex_mxfp8_selftest_wait_timeout(const void* a, const void* b, const void* sfa, const void* sfb,
+                                                void* d, int64_t M, int64_t N, int64_t K, int32_t withhold_stage,
+                                                cutex_stream_t stream) {
+  if (a == nullptr || b == nullptr || sfa == nullptr || sfb == nullptr || d == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  int st = validate_shape(M, N, K);
+  if (st != CUTEX_OK) return st;
+  // The withheld stage must be one every CTA reaches: inside its first tile.
+  if (withhold_stage < 0 || withhold_stage >= K / 128) return CUTEX_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(sfa) || !aligned16(sfb) || !aligned16(d)) return CUTEX_ERR_ALIGN;
+  DeviceState* ds = nullptr;
+  st = current_device_state(&ds);
+  if (st != CUTEX_OK) return st;
+  cutex_gemm_config cfg{};
+  cfg.kernel = CUTEX_KERNEL_1CTA;
+  cfg.tile_n = 128;
+  cfg.stages = 6;
+  cfg.epi_buffers = 1;
+  cfg.sf_buffers = 1;
+  cfg.scheduler = 1;
+  Plan plan{};
+  st = resolve_plan(&cfg, M, N, K, ds->sm_count, &plan, /*plain=*/false);
+  if (st != CUTEX_OK) return st;
+  if (plan.variant == nullptr || plan.variant->fn_fault == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
+  return launch_gemm(plan, dev, a, b, sfa, sfb, d, M, N, K, N, reinterpret_cast<cudaStream_t>(stream), nullptr, 0,
+                     nullptr, nullptr, 0, withhold_stage);
 }
 
 extern "C" int cutex_dense_gemm_v13(const void* a, const void* b, const void* sfa, const void* sfb,

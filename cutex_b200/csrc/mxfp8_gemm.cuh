@@ -78,7 +78,14 @@ struct GemmArgs {
   // that describe the peers' copies of D (NVLink peer memory).
   const CUtensorMap* peer_maps;
   int num_peers;
+  // Error-path self-test builds (kFaultTest) only: the producer issues no copies
+  // for this CTA's K-stage with linear index fault_withhold_kit.
+  int fault_withhold_kit;
 };
+
+// Wait limit of the error-path self-test builds: short enough for a test, far
+// above the time any stage of a small GEMM takes to arrive.
+constexpr uint64_t kFaultTestWaitNs = 1000000ull;  // 1 ms
 
 // In-kernel event trace of the first CTA (pair): each role's recording thread
 // appends (globaltimer ns, event << 56 | tile << 24 | k_block) records to its own
@@ -386,8 +393,14 @@ __device__ __forceinline__ void settle_inflight_copies() {
   while (ptx::globaltimer() - t0 < 50000ull) __nanosleep(1000);
 }
 
+// kFaultTest: the error-path self-test twin (static scheduler only). Every
+// bounded wait gives up after kFaultTestWaitNs, and the producer skips the
+// copies of K-stage args.fault_withhold_kit (and its expect-tx), so the MMA
+// issuer waits for data that never arrives while nothing is in flight for that
+// stage; the roles then time out in turn and the CTA settles, frees TMEM and
+// exits with the error recorded in g_cutex_device_status.
 template <int kCtaGroup, int kTileN, int kStages, int kEpiBufs, int kSFBufs, bool kDynamic,
-          bool kTrace = false, int kEpi = 0>
+          bool kTrace = false, int kEpi = 0, bool kFaultTest = false>
 __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
     mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -396,6 +409,8 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
                       const __grid_constant__ CUtensorMap tmap_d, const GemmArgs args) {
   using C = GemmCfg<kCtaGroup, kTileN, kStages, kEpiBufs, kSFBufs>;
   constexpr bool kPair = kCtaGroup == 2;
+  static_assert(!(kFaultTest && (kDynamic || kTrace || kEpi != 0)), "self-test twin: static, plain epilogue");
+  constexpr uint64_t kLimit = kFaultTest ? kFaultTestWaitNs : ptx::kWaitLimitNs;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = ptx::smem_u32(smem_raw);
@@ -520,12 +535,13 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
         const int s = static_cast<int>(kit % kStages);
         const uint32_t round = kit / kStages;
         tr.rec(kEvProdWait, t, kb);
-        if (!ptx::mbar_wait_warp(empty_bar(s), (round & 1u) ^ 1u, status, kDevTimeoutProducer)) {
+        if (!ptx::mbar_wait_warp<false, kLimit>(empty_bar(s), (round & 1u) ^ 1u, status, kDevTimeoutProducer)) {
           ok = false;
           break;
         }
         tr.rec(kEvProdGo, t, kb);
-        if (ptx::elect_one()) {
+        const bool withheld = kFaultTest && kit == static_cast<uint32_t>(args.fault_withhold_kit);
+        if (!withheld && ptx::elect_one()) {
           const uint64_t pol = ptx::policy_evict_normal();
           if (leader) ptx::mbar_arrive_expect_tx(full_bar(s), C::kTxBytes);
           const uint32_t sa = smem + C::kOffA + s * C::kABytes;
@@ -553,8 +569,8 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
     // Drain: every stage this CTA filled has been consumed by the MMAs.
     for (int i = 0; ok && i < kStages; ++i) {
       const uint32_t k2 = kit + i;
-      ok = ptx::mbar_wait_warp(empty_bar(static_cast<int>(k2 % kStages)), ((k2 / kStages) & 1u) ^ 1u, status,
-                               kDevTimeoutProducer);
+      ok = ptx::mbar_wait_warp<false, kLimit>(empty_bar(static_cast<int>(k2 % kStages)), ((k2 / kStages) & 1u) ^ 1u,
+                                              status, kDevTimeoutProducer);
     }
     if (!ok) settle_inflight_copies();
     tr.rec(kEvEnd, 0, 0);
@@ -577,12 +593,12 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
         tr.rec(kEvMmaAccWait, t, 0);
         if constexpr (C::kOverlap) {
           if (it >= 1)
-            ok = ptx::mbar_wait_warp<kPair>(acc_empty_bar((it - 1) & 1), ((it - 1) >> 1) & 1, status,
-                                            kDevTimeoutAccEmpty);
+            ok = ptx::mbar_wait_warp<kPair, kLimit>(acc_empty_bar((it - 1) & 1), ((it - 1) >> 1) & 1, status,
+                                                    kDevTimeoutAccEmpty);
         } else {
           if (it >= 2)
-            ok = ptx::mbar_wait_warp<kPair>(acc_empty_bar(buf), ((it - 2) >> 1) & 1, status,
-                                            kDevTimeoutAccEmpty);
+            ok = ptx::mbar_wait_warp<kPair, kLimit>(acc_empty_bar(buf), ((it - 2) >> 1) & 1, status,
+                                                    kDevTimeoutAccEmpty);
         }
         if (!ok) break;
         tr.rec(kEvMmaAccGo, t, 0);
@@ -591,7 +607,7 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
         for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
           const int s = static_cast<int>(kit % kStages);
           tr.rec(kEvMmaFullWait, t, kb);
-          if (!ptx::mbar_wait_warp(full_bar(s), (kit / kStages) & 1u, status, kDevTimeoutMma)) {
+          if (!ptx::mbar_wait_warp<false, kLimit>(full_bar(s), (kit / kStages) & 1u, status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
@@ -653,7 +669,7 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
       const int n_col = nt * kTileN;
       const int buf = it & 1;
       tr.rec(kEvEpiWait, t, 0);
-      if (!ptx::mbar_wait(acc_full_bar(buf), (it >> 1) & 1, status, kDevTimeoutEpilogue)) break;
+      if (!ptx::mbar_wait<false, kLimit>(acc_full_bar(buf), (it >> 1) & 1, status, kDevTimeoutEpilogue)) break;
       const unsigned long long t_go = tr.stamp();
       unsigned long long t_loaded = 0;
       ptx::tc_fence_after();

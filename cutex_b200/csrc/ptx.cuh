@@ -125,15 +125,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase of the given parity to complete. On timeout the
-// first error code wins in *status and false is returned.
-template <bool kClusterScope = false>
+// first error code wins in *status and false is returned. kLimitNs is the
+// wall-time limit (the error-path self-test builds use a short one).
+template <bool kClusterScope = false, uint64_t kLimitNs = kWaitLimitNs>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status, int code) {
   if (mbar_try_wait<kClusterScope>(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait<kClusterScope>(bar, parity)) return true;
-    if ((++spins & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+    if ((++spins & 63u) == 0 && globaltimer() - t0 > kLimitNs) {
       atomicCAS(status, 0, code);
       return false;
     }
@@ -151,9 +152,9 @@ __device__ __forceinline__ bool elect_one() {
 
 // mbar_wait executed by every lane of a converged warp; the result is made
 // warp-uniform so the caller's control flow cannot diverge on a timeout.
-template <bool kClusterScope = false>
+template <bool kClusterScope = false, uint64_t kLimitNs = kWaitLimitNs>
 __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int* status, int code) {
-  const bool ok = mbar_wait<kClusterScope>(bar, parity, status, code);
+  const bool ok = mbar_wait<kClusterScope, kLimitNs>(bar, parity, status, code);
   return __all_sync(0xffffffffu, ok) != 0;
 }
 

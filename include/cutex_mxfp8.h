@@ -198,6 +198,23 @@ CUTEX_API int cutex_mxfp8_gemm_allgather(const void* a, const void* b, const voi
                                          int32_t num_peers, const cutex_gemm_config* cfg, cutex_stream_t stream);
 
 /*
+ * Self-test of the device error path. No counterpart in the reference, whose
+ * only protection against a stuck kernel is a host-side timeout.
+ * Runs the GEMM D[M,N] (row stride N) on a build of the single-CTA, static
+ * kernel whose bounded waits give up after 1 ms (2 s in every other build)
+ * and whose TMA producer issues no copies for each CTA's K-stage number
+ * withhold_stage (0 <= withhold_stage < K/128; its first tile). The MMA issuer
+ * then waits for data that never arrives while nothing is in flight for that
+ * stage; every role times out in turn, lets its in-flight copies land, frees
+ * TMEM and exits. Afterwards cutex_last_device_status(stream) must return
+ * CUTEX_ERR_TIMEOUT (and clears the word); D is left unwritten, and the device
+ * stays usable for later launches.
+ */
+CUTEX_API int cutex_mxfp8_selftest_wait_timeout(const void* a, const void* b, const void* sfa, const void* sfb,
+                                                void* d, int64_t M, int64_t N, int64_t K, int32_t withhold_stage,
+                                                cutex_stream_t stream);
+
+/*
  * Resolve a configuration for a shape without launching anything.
  * Replaces the host-side resource accounting of dense_gemm_v13
  * (cutex/kernels/dense_gemm_v13.py:1095-1239: SMEM layouts, tma_bytes, grid).

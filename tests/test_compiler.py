@@ -191,3 +191,19 @@ def test_gemm_launcher_carries_the_device_health_probe():
     from cutex_b200.kernels.dense_gemm import mxfp8_gemm_launch
 
     assert callable(getattr(mxfp8_gemm_launch, DEVICE_STATUS_ATTRIBUTE))
+
+
+def test_launcher_config_field_named_kernel_binds():
+    # The GEMM launcher's config has a field called `kernel`; binding and compiling must pass it through.
+    def launcher(x, *, kernel=0, tile_n=0):
+        return (x, kernel, tile_n)
+
+    assert bind_config(launcher, 1, kernel=3, tile_n=128)(1) == (1, 3, 128)
+
+    @autotune(configs=[Config({"kernel": 1}, name="one"), Config({"kernel": 2}, name="two")], key=["x"])
+    def tuned(x, *, kernel=0):
+        return kernel
+
+    out = compile(tuned, 5, cache_path=None,
+                  do_bench=lambda bound, *a, warmup=0, rep=0, **k: float(bound(*a, **k)))
+    assert out.best_config.name == "one" and out(5) == 1
