@@ -40,7 +40,8 @@ class GemmConfigC(ctypes.Structure):
         ("epi_buffers", ctypes.c_int32),
         ("sf_buffers", ctypes.c_int32),
         ("scheduler", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 6),
+        ("l2_prefetch", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 5),
     ]
 
 

@@ -37,10 +37,64 @@ struct DeviceState {
 std::mutex g_mutex;
 DeviceState g_devices[kMaxDevices];
 
+// Per-device caches (kernel attributes, occupancy, the no-allocation scratch
+// address, the host pipeline's streams) are only valid inside the CUDA context
+// they were filled in. Each device has an epoch that changes whenever the
+// current context of that device is a different one (a device reset destroys
+// the primary context; its successor gets a new, never reused, context ID), and
+// every cache records the epoch it was filled in. g_epoch is guarded by g_mutex.
+unsigned long long g_ctx_id[kMaxDevices];
+unsigned g_epoch[kMaxDevices];
+
+unsigned long long current_context_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_ctx = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  }();
+  static PFN_cuCtxGetId_v12000 get_id = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  }();
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_ctx == nullptr || get_id == nullptr || get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// With g_mutex held: the device's epoch, advanced if its current context changed.
+// Before the runtime has created a context there is none to ask about (ID 0):
+// the first real ID seen then advances the epoch once. Only driver queries are
+// made here, nothing that a stream capture forbids.
+unsigned device_epoch_locked(int dev) {
+  const unsigned long long id = current_context_id();
+  if (g_epoch[dev] == 0 || (id != 0 && id != g_ctx_id[dev])) {
+    g_ctx_id[dev] = id;
+    ++g_epoch[dev];
+    g_devices[dev].ready = false;
+  }
+  return g_epoch[dev];
+}
+
+unsigned device_epoch(int dev) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  return device_epoch_locked(dev);
+}
+
 int current_device_state(DeviceState** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CUTEX_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_mutex);
+  device_epoch_locked(dev);
   DeviceState& st = g_devices[dev];
   if (!st.ready) {
     if (cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
@@ -166,15 +220,18 @@ int launch_quantize_columnwise_t(const CUtensorMap& tmap, const CUtensorMap& tma
   // Per device (the shared-memory attribute is set in each device's context):
   // resident CTAs per SM, for one wave of persistent CTAs.
   static int per_sm[kMaxDevices] = {};
+  static unsigned per_sm_epoch[kMaxDevices] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CUTEX_ERR_CUDA;
   int resident = 0;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (per_sm[dev] == 0) {
+    const unsigned epoch = device_epoch_locked(dev);
+    if (per_sm_epoch[dev] != epoch) {
       if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
         return CUTEX_ERR_CUDA;
       per_sm[dev] = resident_ctas(fn, 256, C::kSmemBytes);
+      per_sm_epoch[dev] = epoch;
     }
     resident = per_sm[dev];
   }
@@ -198,11 +255,13 @@ struct Variant {
   const void* fn_trace;   // instrumented twin (cutex_mxfp8_gemm_trace), or null
   const void* fn_epi[4];  // fused-epilogue twins: [1] BF16 out, [2] E4M3 + scales out, [3] all-gather
   const void* fn_fault;   // error-path self-test twin (cutex_mxfp8_selftest_wait_timeout), or null
-  bool attr_set_trace[kMaxDevices];
-  bool attr_set_fault[kMaxDevices];
-  bool attr_set[kMaxDevices];
-  bool attr_set_epi[4][kMaxDevices];
+  // Epoch (device_epoch) in which each build's shared-memory attribute was set.
+  unsigned attr_set_trace[kMaxDevices];
+  unsigned attr_set_fault[kMaxDevices];
+  unsigned attr_set[kMaxDevices];
+  unsigned attr_set_epi[4][kMaxDevices];
   int max_clusters[kMaxDevices];
+  unsigned max_clusters_epoch[kMaxDevices];
 };
 
 template <int CG, int BN, int S, int E, int F, bool D, bool T = false, bool X = false, bool Q = false>
@@ -263,7 +322,7 @@ Variant* find_variant(int cg, int bn, int stages, int epi, int sfb, int dynamic)
 struct SkinnyVariant {
   int npad, stages, tiles, smem_bytes;
   const void* fn;
-  bool attr_set[kMaxDevices];
+  unsigned attr_set[kMaxDevices];  // epoch in which the shared-memory attribute was set
 };
 
 template <int NP, int S, int T = 1>
@@ -301,6 +360,7 @@ struct Plan {
   int dp_tiles;               // skinny stream-K: tiles taken whole before the split range
   int64_t workspace_bytes;    // skinny stream-K: partial slots + tile counters
   int64_t ws_partials_bytes;  // offset of the counters inside the workspace
+  int l2_prefetch;            // tile kernels: L2 prefetch distance in K-stages (0 = none)
 };
 
 // Skinny stream-K workspace layout, fixed per device so that one workspace can
@@ -338,7 +398,7 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   if (cfg.kernel < 0 || cfg.kernel > CUTEX_KERNEL_SKINNY || cfg.stages < 0 || cfg.raster_group < 0 ||
       cfg.max_ctas < 0 || cfg.split_k < 0 || cfg.epi_buffers < 0 || cfg.epi_buffers > 2 ||
       cfg.sf_buffers < 0 || cfg.sf_buffers > 4 || cfg.scheduler < 0 || cfg.scheduler > 1 ||
-      (cfg.raster_along_n != 0 && cfg.raster_along_n != 1))
+      (cfg.raster_along_n != 0 && cfg.raster_along_n != 1) || cfg.l2_prefetch < 0 || cfg.l2_prefetch > 32)
     return CUTEX_ERR_INVALID_ARGUMENT;
   if (cfg.tile_n != 0 && cfg.tile_n != 128 && cfg.tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
   int kernel = cfg.kernel;
@@ -365,6 +425,7 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   plan->dp_tiles = 0;
   plan->workspace_bytes = 0;
   plan->ws_partials_bytes = 0;
+  plan->l2_prefetch = cfg.l2_prefetch;
   if (kernel == CUTEX_KERNEL_SKINNY) {
     // 0 = stream-K (library choice of full data-parallel waves), 1 = no split,
     // 2 = pure stream-K, 3 = full data-parallel waves + stream-K remainder.
@@ -468,16 +529,18 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
   if (!encode_operand(&ta, a, M, K, 128) || !encode_operand(&tb, b, N, K, v->tile_n / cg) ||
       !encode_scales(&tsa, sfa, M, K, 1) || !encode_scales(&tsb, sfb, N, K, v->tile_n / 128) || !out_ok)
     return CUTEX_ERR_CUDA;
+  unsigned epoch = 0;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    bool& set = fault ? v->attr_set_fault[dev]
-                : traced ? v->attr_set_trace[dev]
-                         : (epi_kind != 0 ? v->attr_set_epi[epi_kind][dev] : v->attr_set[dev]);
-    if (!set) {
+    epoch = device_epoch_locked(dev);
+    unsigned& set = fault ? v->attr_set_fault[dev]
+                    : traced ? v->attr_set_trace[dev]
+                             : (epi_kind != 0 ? v->attr_set_epi[epi_kind][dev] : v->attr_set[dev]);
+    if (set != epoch) {
       if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v->smem_bytes) !=
           cudaSuccess)
         return CUTEX_ERR_CUDA;
-      set = true;
+      set = epoch;
     }
   }
   GemmArgs args{};
@@ -496,6 +559,7 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
   args.peer_maps = peer_maps;
   args.num_peers = num_peers;
   args.fault_withhold_kit = fault_kit;
+  args.l2_prefetch = plan.l2_prefetch;
   if (epi != nullptr) {
     args.alpha = epi->alpha;
     args.beta = epi->beta;
@@ -523,7 +587,7 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
     int max_clusters = 0;
     {
       std::lock_guard<std::mutex> lock(g_mutex);
-      max_clusters = v->max_clusters[dev];
+      if (v->max_clusters_epoch[dev] == epoch) max_clusters = v->max_clusters[dev];
     }
     if (max_clusters == 0) {
       if (cudaOccupancyMaxActiveClusters(&max_clusters, fn, &lc) != cudaSuccess ||
@@ -531,6 +595,7 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
         return CUTEX_ERR_CUDA;
       std::lock_guard<std::mutex> lock(g_mutex);
       v->max_clusters[dev] = max_clusters;
+      v->max_clusters_epoch[dev] = epoch;
     }
     if (!v->dynamic && plan.grid_ctas > 2 * max_clusters)
       lc.gridDim.x = static_cast<unsigned>(2 * max_clusters);
@@ -558,11 +623,12 @@ int launch_skinny(const Plan& plan, int dev, const void* a, const void* b, const
     return CUTEX_ERR_CUDA;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (!v->attr_set[dev]) {
+    const unsigned epoch = device_epoch_locked(dev);
+    if (v->attr_set[dev] != epoch) {
       if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v->smem_bytes) !=
           cudaSuccess)
         return CUTEX_ERR_CUDA;
-      v->attr_set[dev] = true;
+      v->attr_set[dev] = epoch;
     }
   }
   SkinnyArgs args{};
@@ -998,6 +1064,7 @@ namespace cutex {
 namespace {
 
 void* g_static_scratch_ptr[kMaxDevices];
+unsigned g_static_scratch_epoch[kMaxDevices];  // device_epoch in which the address was fetched
 
 }  // namespace
 }  // namespace cutex
@@ -1020,15 +1087,19 @@ extern "C" int cutex_mxfp8_gemm_skinny_static(const void* a, const void* b, cons
   if (cudaGetDevice(&dev) != cudaSuccess) return CUTEX_ERR_CUDA;
 
   // Set-up, once per device and with that device current: in host code the
-  // array's name is only a host-side stand-in, so fetch its device address.
+  // array's name is only a host-side stand-in, so fetch its device address. The
+  // address is fetched again if the device's context changed since (after a
+  // device reset the module, and the array, are loaded anew).
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (g_static_scratch_ptr[dev] == nullptr) {
+    const unsigned epoch = device_epoch_locked(dev);
+    if (g_static_scratch_ptr[dev] == nullptr || g_static_scratch_epoch[dev] != epoch) {
       void* p = nullptr;
       if (cudaGetSymbolAddress(&p, g_skinny_static_scratch) != cudaSuccess || p == nullptr)
         return CUTEX_ERR_CUDA;
       g_static_scratch_ptr[dev] = p;
+      g_static_scratch_epoch[dev] = epoch;
     }
     scratch = g_static_scratch_ptr[dev];
   }
@@ -1073,6 +1144,7 @@ struct HostPipe {
   cudaEvent_t start = nullptr, end_h2d = nullptr, end_comp = nullptr, end_d2h = nullptr;
   cudaEvent_t a_in[kMaxHostBlocks] = {}, b_in[kMaxHostBlocks] = {};
   cudaEvent_t done[kMaxHostBlocks * kMaxHostBlocks] = {};
+  unsigned epoch = 0;  // device_epoch the streams and events were created in
 };
 
 HostPipe g_pipes[kMaxDevices];
@@ -1080,6 +1152,12 @@ std::mutex g_pipe_mutex;
 
 int host_pipe(int dev, HostPipe** out) {
   HostPipe& p = g_pipes[dev];
+  const unsigned epoch = device_epoch(dev);
+  if (p.epoch != epoch) {
+    // Created in a context that no longer exists: those handles are gone with it.
+    p = HostPipe{};
+    p.epoch = epoch;
+  }
   if (!p.ready) {
     const unsigned ev_flags = cudaEventDisableTiming;
     bool ok = cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking) == cudaSuccess &&

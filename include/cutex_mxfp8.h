@@ -75,7 +75,10 @@ typedef struct cutex_gemm_config {
   int32_t sf_buffers;     /* rotating scale-factor TMEM buffers (1, 2 or 4) */
   int32_t scheduler;      /* 0: dynamic (one cluster per tile, idle clusters take over pending
                              ones through cluster launch control); 1: static persistent grid */
-  int32_t reserved[6];    /* must be zero */
+  int32_t l2_prefetch;    /* tile kernels: also prefetch each CTA's A and B tiles this many
+                             K-stages ahead of its loads into L2 (0 = none, at most 32;
+                             ignored by the skinny kernel) */
+  int32_t reserved[5];    /* must be zero */
 } cutex_gemm_config;
 
 /* What a launch with this configuration would do (filled by cutex_mxfp8_query). */
@@ -294,9 +297,11 @@ CUTEX_API int cutex_mxfp8_quantize_columnwise(const void* x, int32_t x_dtype, in
  *   M <= 128 (else CUTEX_ERR_SHAPE); N <= 2,097,152 and at most 160 SMs (else
  *   CUTEX_ERR_WORKSPACE). The first call on a device performs one-time set-up
  *   (it looks up the scratch array's device address); make that first call
- *   before any stream capture. Every call shares the one scratch array: calls
- *   that may overlap on the GPU (different streams, or different host threads)
- *   race and must be serialised by the caller.
+ *   before any stream capture. The set-up is repeated, by the next call, when
+ *   the device's CUDA context has changed since (a device reset). Every call
+ *   shares the one scratch array: calls that may overlap on the GPU (different
+ *   streams, or different host threads) race and must be serialised by the
+ *   caller.
  */
 CUTEX_API int cutex_mxfp8_gemm_skinny_static(const void* a, const void* b, const void* sfa,
                                              const void* sfb, void* d, int64_t M, int64_t N,

@@ -8,10 +8,8 @@ the status word, the word is cleared by the read, the output is untouched, and
 ordinary GEMMs on the same device still pass the oracle afterwards.
 """
 
-import ctypes
 import time
 
-import numpy as np
 import pytest
 import torch
 
@@ -60,5 +58,4 @@ def test_self_test_rejects_a_stage_outside_the_first_tile():
     for bad in (-1, K // 128):
         assert _launch(t, t, t, t, d, M, N, K, bad, stream) == _lib.CUTEX_ERR_INVALID_ARGUMENT
     assert _lib.load().cutex_last_device_status(stream) == _lib.CUTEX_OK
-    assert np.all(d.cpu().numpy() == 0)
-    assert ctypes.sizeof(ctypes.c_int32) == 4
+    assert not d.any().item()  # nothing was launched
