@@ -500,7 +500,7 @@ def bench_cutex(args):
                      "frac": sustained_value / world / peak_s, "peak": peak_s, "peak_source": peak_s_src}
         if clocks2.get("power_w_median"):
             # Energy per GEMM at the power cap: median board power x time per launch (per GPU).
-            sustained["joules_per_gemm"] = clocks2["power_w_median"] * float(ts[0]) / launches
+            sustained["joules_per_gemm"] = clocks2["power_w_median"] * (float(ts[0]) / 1e3) / launches
     # Back-to-back launches in one graph: the average launch duration is the
     # timed interval over the launch count (inter-kernel gaps included).
     t = torch.tensor([elapsed_ms, elapsed_ms / args.steps], dtype=torch.float64, device=device)

@@ -40,8 +40,7 @@ class GemmConfigC(ctypes.Structure):
         ("epi_buffers", ctypes.c_int32),
         ("sf_buffers", ctypes.c_int32),
         ("scheduler", ctypes.c_int32),
-        ("l2_prefetch", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 5),
+        ("reserved", ctypes.c_int32 * 6),
     ]
 
 

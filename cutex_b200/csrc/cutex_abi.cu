@@ -360,7 +360,6 @@ struct Plan {
   int dp_tiles;               // skinny stream-K: tiles taken whole before the split range
   int64_t workspace_bytes;    // skinny stream-K: partial slots + tile counters
   int64_t ws_partials_bytes;  // offset of the counters inside the workspace
-  int l2_prefetch;            // tile kernels: L2 prefetch distance in K-stages (0 = none)
 };
 
 // Skinny stream-K workspace layout, fixed per device so that one workspace can
@@ -398,7 +397,7 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   if (cfg.kernel < 0 || cfg.kernel > CUTEX_KERNEL_SKINNY || cfg.stages < 0 || cfg.raster_group < 0 ||
       cfg.max_ctas < 0 || cfg.split_k < 0 || cfg.epi_buffers < 0 || cfg.epi_buffers > 2 ||
       cfg.sf_buffers < 0 || cfg.sf_buffers > 4 || cfg.scheduler < 0 || cfg.scheduler > 1 ||
-      (cfg.raster_along_n != 0 && cfg.raster_along_n != 1) || cfg.l2_prefetch < 0 || cfg.l2_prefetch > 32)
+      (cfg.raster_along_n != 0 && cfg.raster_along_n != 1))
     return CUTEX_ERR_INVALID_ARGUMENT;
   if (cfg.tile_n != 0 && cfg.tile_n != 128 && cfg.tile_n != 256) return CUTEX_ERR_INVALID_ARGUMENT;
   int kernel = cfg.kernel;
@@ -425,7 +424,6 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   plan->dp_tiles = 0;
   plan->workspace_bytes = 0;
   plan->ws_partials_bytes = 0;
-  plan->l2_prefetch = cfg.l2_prefetch;
   if (kernel == CUTEX_KERNEL_SKINNY) {
     // 0 = stream-K (library choice of full data-parallel waves), 1 = no split,
     // 2 = pure stream-K, 3 = full data-parallel waves + stream-K remainder.
@@ -559,7 +557,6 @@ int launch_gemm(const Plan& plan, int dev, const void* a, const void* b, const v
   args.peer_maps = peer_maps;
   args.num_peers = num_peers;
   args.fault_withhold_kit = fault_kit;
-  args.l2_prefetch = plan.l2_prefetch;
   if (epi != nullptr) {
     args.alpha = epi->alpha;
     args.beta = epi->beta;

@@ -81,10 +81,6 @@ struct GemmArgs {
   // Error-path self-test builds (kFaultTest) only: the producer issues no copies
   // for this CTA's K-stage with linear index fault_withhold_kit.
   int fault_withhold_kit;
-  // > 0: after its loads of K-stage kb, the producer also prefetches its A and B
-  // tiles of K-stage kb + l2_prefetch (same tile) into L2, so that TMA loads of
-  // operands whose lines left the L2 do not wait for DRAM.
-  int l2_prefetch;
 };
 
 // Wait limit of the error-path self-test builds: short enough for a test, far
@@ -565,11 +561,6 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
             ptx::tma_load_2d(sb, &tmap_b, fb, kx, b_row, pol);
             ptx::tma_load_3d(ssfa, &tmap_sfa, fb, 0, kb, sfa_blk, pol);
             ptx::tma_load_3d(ssfb, &tmap_sfb, fb, 0, kb, sfb_blk, pol);
-          }
-          if (args.l2_prefetch > 0 && kb + args.l2_prefetch < args.num_k_blocks) {
-            const int px = (kb + args.l2_prefetch) * 128;
-            ptx::tma_prefetch_2d(&tmap_a, px, a_row);
-            ptx::tma_prefetch_2d(&tmap_b, px, b_row);
           }
         }
         __syncwarp();

@@ -174,14 +174,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, uint3
       : "memory");
 }
 
-// Bulk prefetch of one tile of a tensor map into L2 (no shared-memory
-// destination, no completion to wait for).
-__device__ __forceinline__ void tma_prefetch_2d(const void* map, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint32_t bar, int32_t x,
                                             int32_t y, int32_t z, uint64_t cache_hint) {
   asm volatile(

@@ -45,7 +45,6 @@ class GemmConfig:
     epi_buffers: int = 0
     sf_buffers: int = 0
     scheduler: int = 0
-    l2_prefetch: int = 0
 
     def to_c(self) -> _lib.GemmConfigC:
         return _lib.make_config(**asdict(self))
@@ -335,11 +334,11 @@ GEMM_CONFIGS = (
 @autotune(configs=GEMM_CONFIGS, key=["m", "n", "k", "target"], warmup=3, rep=10)
 def mxfp8_gemm_launch(a, b, sfa, sfb, out, m, n, k, target, stream=None, *, kernel=0, tile_n=0,
                       stages=0, raster_group=0, raster_along_n=0, split_k=0, max_ctas=0, epi_buffers=0,
-                      sf_buffers=0, scheduler=0, l2_prefetch=0):
+                      sf_buffers=0, scheduler=0):
     """Autotunable launcher: ``cutex_b200.compile(mxfp8_gemm_launch, a, b, sfa, sfb, out, m, n, k, target)``."""
 
     cfg = GemmConfig(kernel, tile_n, stages, raster_group, raster_along_n, split_k, max_ctas, epi_buffers,
-                     sf_buffers, scheduler, l2_prefetch)
+                     sf_buffers, scheduler)
     return dense_gemm(a, b, sfa, sfb, out, stream=stream, config=cfg)
 
 

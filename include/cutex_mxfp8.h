@@ -75,10 +75,7 @@ typedef struct cutex_gemm_config {
   int32_t sf_buffers;     /* rotating scale-factor TMEM buffers (1, 2 or 4) */
   int32_t scheduler;      /* 0: dynamic (one cluster per tile, idle clusters take over pending
                              ones through cluster launch control); 1: static persistent grid */
-  int32_t l2_prefetch;    /* tile kernels: also prefetch each CTA's A and B tiles this many
-                             K-stages ahead of its loads into L2 (0 = none, at most 32;
-                             ignored by the skinny kernel) */
-  int32_t reserved[5];    /* must be zero */
+  int32_t reserved[6];    /* must be zero */
 } cutex_gemm_config;
 
 /* What a launch with this configuration would do (filled by cutex_mxfp8_query). */
