@@ -105,6 +105,71 @@ __device__ __forceinline__ void finish_group(const float (&v)[8], int64_t rows, 
   }
 }
 
+// One 8-element bf16 group (4 packed words) of a 1x32 block held by a quad:
+// the block amax on packed 16-bit magnitudes (a bf16 magnitude's bit pattern
+// orders like its value, and its exponent field is the fp32 one), the scale
+// byte, and the 8 E4M3 codes. Same rule and bits as finish_group, with fewer
+// instructions: the bf16 form of the quantiser is issue-bound, not HBM-bound.
+__device__ __forceinline__ uint2 quantize_bf16_group(const uint4 w, unsigned quad, uint32_t& sbyte) {
+  const uint32_t m4 = __vmaxu2(__vmaxu2(w.x & 0x7FFF7FFFu, w.y & 0x7FFF7FFFu),
+                               __vmaxu2(w.z & 0x7FFF7FFFu, w.w & 0x7FFF7FFFu));
+  uint32_t amax = max(m4 & 0xFFFFu, m4 >> 16);
+  amax = max(amax, __shfl_xor_sync(quad, amax, 1));
+  amax = max(amax, __shfl_xor_sync(quad, amax, 2));
+  const bool nonfinite = amax >= 0x7F80u;  // an infinity or NaN in the block
+  const uint32_t exp_field = amax >> 7;
+  sbyte = nonfinite ? 0xFFu : (exp_field >= 8u ? exp_field - 8u : 0u);
+  const float mult = __uint_as_float((254u - (nonfinite ? 127u : sbyte)) << 23);  // 2^(127 - sbyte), exact
+  const uint32_t c0 = fp8x2(__uint_as_float(w.x << 16) * mult, __uint_as_float(w.x & 0xFFFF0000u) * mult);
+  const uint32_t c1 = fp8x2(__uint_as_float(w.y << 16) * mult, __uint_as_float(w.y & 0xFFFF0000u) * mult);
+  const uint32_t c2 = fp8x2(__uint_as_float(w.z << 16) * mult, __uint_as_float(w.z & 0xFFFF0000u) * mult);
+  const uint32_t c3 = fp8x2(__uint_as_float(w.w << 16) * mult, __uint_as_float(w.w & 0xFFFF0000u) * mult);
+  const uint2 out = make_uint2(c0 | (c1 << 16), c2 | (c3 << 16));
+  return nonfinite ? make_uint2(0u, 0u) : out;
+}
+
+// bf16 input: rows walked as in the fp32 form (whole rows per CTA, threads along
+// the row, 8 groups = 128 bytes of loads per thread before any is quantised),
+// with the row's bounds, addresses and scale-row offset computed once per row.
+__device__ __forceinline__ void quantize_rows_bf16(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t K,
+                                                   int64_t ldx, uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  constexpr int kU = 8;
+  const int k8 = static_cast<int>(K >> 3);  // 8-element groups per row (K < 2^31)
+  const int64_t rows_pad = (rows + 127) & ~int64_t{127};
+  const unsigned quad = 0xFu << (threadIdx.x & 28u);
+  const int bd = static_cast<int>(blockDim.x);
+  for (int64_t r = blockIdx.x; r < rows_pad; r += gridDim.x) {
+    uint8_t* sf_row = sf + ((r >> 7) * (K >> 7)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4;
+    if (r >= rows) {  // padding row of the last 128-row scale block: scale 0x00, no codes
+      for (int c = threadIdx.x; c < (k8 >> 2); c += bd) sf_row[((c >> 2) << 9) + (c & 3)] = 0;
+      continue;
+    }
+    const uint4* xr = reinterpret_cast<const uint4*>(x + r * ldx);
+    uint2* qr = reinterpret_cast<uint2*>(q + r * K);
+    for (int g0 = threadIdx.x; g0 < k8; g0 += bd * kU) {
+      uint4 raw[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int g = g0 + u * bd;
+        raw[u] = g < k8 ? __ldcs(xr + g) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int g = g0 + u * bd;
+        if (g < k8) {  // k8 and bd are multiples of 4: a quad takes this branch together
+          uint32_t sbyte;
+          const uint2 codes = quantize_bf16_group(raw[u], quad, sbyte);
+          qr[g] = codes;
+          if ((g & 3) == 0) {
+            const int c = g >> 2;
+            sf_row[((c >> 2) << 9) + (c & 3)] = static_cast<uint8_t>(sbyte);
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int kDtype>  // 0: float32, 1: bfloat16
 __global__ void __launch_bounds__(256) mxfp8_quantize_kernel(const void* __restrict__ x, int64_t rows,
                                                              int64_t K, int64_t ldx,
@@ -114,14 +179,15 @@ __global__ void __launch_bounds__(256) mxfp8_quantize_kernel(const void* __restr
   const int64_t rows_pad = (rows + 127) & ~int64_t{127};
   // blockDim.x and k8 are multiples of 4, so the four lanes of a quad always
   // take the same trip through the row loop.
+  if constexpr (kDtype == 1) {
+    quantize_rows_bf16(static_cast<const __nv_bfloat16*>(x), rows, K, ldx, q, sf);
+    return;
+  }
   const unsigned quad = 0xFu << (threadIdx.x & 28u);
   // kU groups per thread and step, all loaded (as raw words, 32 registers)
-  // before any is quantised: 128 bytes of loads in flight per thread for both
-  // input types (4 fp32 groups or 8 bf16 groups), which is what the HBM
-  // latency needs at the occupancy these register counts allow. (A bf16 form
-  // with 64 bytes per thread, software-pipelined over steps, measured 0.72 of
-  // the HBM copy rate at 16384 x 16384; the fp32 form 0.94.)
-  constexpr int kU = kDtype == 0 ? 4 : 8;
+  // before any is quantised: 128 bytes of loads in flight per thread, which is
+  // what the HBM latency needs at the occupancy this register count allows.
+  constexpr int kU = 4;
   const int64_t step = static_cast<int64_t>(blockDim.x) * kU;
   for (int64_t r = blockIdx.x; r < rows_pad; r += gridDim.x) {
     for (int64_t g0 = threadIdx.x; g0 < k8; g0 += step) {
