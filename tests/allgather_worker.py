@@ -23,13 +23,21 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
-from cutex_b200.kernels import dense_gemm  # noqa: E402
+from cutex_b200.kernels import GemmConfig, dense_gemm  # noqa: E402
 from cutex_b200.sharding import FusedAllGatherGemm, ShardedHostGemm, scale_rows_slice, shard_bounds  # noqa: E402
 from tests.gpu_helpers import O, make_operands  # noqa: E402
 
 
 def _bits(t):
     return t.contiguous().view(torch.int16)
+
+
+def fused_family(M, n_local):
+    """The kernel cutex_mxfp8_gemm_allgather chooses for an [M, n_local] slice (its AUTO rule)."""
+
+    if M > 128 and n_local % 256 == 0:
+        return GemmConfig(kernel=2)
+    return GemmConfig(kernel=1, tile_n=128)
 
 
 def main() -> int:
@@ -48,7 +56,11 @@ def main() -> int:
             ta, tsa = torch.from_numpy(a).to(dev), torch.from_numpy(sfa).to(dev)
             tb, tsb = torch.from_numpy(b).to(dev), torch.from_numpy(sfb).to(dev)
             ref = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-            dense_gemm(ta, tb, tsa, tsb, ref)
+            # The bitwise reference runs the tile kernel the fused path picks for this rank's
+            # slice: every output element is then the same MMA sequence in one accumulator.
+            # (AUTO would take the split-K kernel for M <= 128, whose split tiles round
+            # differently.)
+            dense_gemm(ta, tb, tsa, tsb, ref, config=fused_family(M, shard.n))
             sets.append({"np": (a, sfa, b, sfb), "dev": (ta, tsa, tsb), "b_loc": tb[shard.n0:shard.n1].contiguous(),
                          "sfb_loc": tsb[s0:s1].contiguous(), "ref": ref})
         torch.cuda.synchronize()
