@@ -105,67 +105,90 @@ __device__ __forceinline__ void finish_group(const float (&v)[8], int64_t rows, 
   }
 }
 
-// One 8-element bf16 group (4 packed words) of a 1x32 block held by a quad:
-// the block amax on packed 16-bit magnitudes (a bf16 magnitude's bit pattern
-// orders like its value, and its exponent field is the fp32 one), the scale
-// byte, and the 8 E4M3 codes. Same rule and bits as finish_group, with fewer
-// instructions: the bf16 form of the quantiser is issue-bound, not HBM-bound.
-__device__ __forceinline__ uint2 quantize_bf16_group(const uint4 w, unsigned quad, uint32_t& sbyte) {
-  const uint32_t m4 = __vmaxu2(__vmaxu2(w.x & 0x7FFF7FFFu, w.y & 0x7FFF7FFFu),
-                               __vmaxu2(w.z & 0x7FFF7FFFu, w.w & 0x7FFF7FFFu));
-  uint32_t amax = max(m4 & 0xFFFFu, m4 >> 16);
-  amax = max(amax, __shfl_xor_sync(quad, amax, 1));
-  amax = max(amax, __shfl_xor_sync(quad, amax, 2));
+// 16 bf16 elements (two 8-element groups, 8 packed words) of a 1x32 block held
+// by a lane pair: the block amax on packed 16-bit magnitudes (a bf16
+// magnitude's bit pattern orders like its value, and its exponent field is the
+// fp32 one), the scale byte, and the 16 E4M3 codes. Same rule and bits as
+// finish_group, with fewer instructions per element: the bf16 form of the
+// quantiser is issue-bound, not HBM-bound, with 8 elements per lane.
+__device__ __forceinline__ uint32_t bf16x2_e4m3x2(uint32_t w, float mult) {
+  return fp8x2(__uint_as_float(w << 16) * mult, __uint_as_float(w & 0xFFFF0000u) * mult);
+}
+
+__device__ __forceinline__ uint4 quantize_bf16_half_block(const uint4 a, const uint4 b, unsigned pair,
+                                                          uint32_t& sbyte) {
+  const uint32_t m = __vmaxu2(__vmaxu2(__vmaxu2(a.x & 0x7FFF7FFFu, a.y & 0x7FFF7FFFu),
+                                       __vmaxu2(a.z & 0x7FFF7FFFu, a.w & 0x7FFF7FFFu)),
+                              __vmaxu2(__vmaxu2(b.x & 0x7FFF7FFFu, b.y & 0x7FFF7FFFu),
+                                       __vmaxu2(b.z & 0x7FFF7FFFu, b.w & 0x7FFF7FFFu)));
+  uint32_t amax = max(m & 0xFFFFu, m >> 16);
+  amax = max(amax, __shfl_xor_sync(pair, amax, 1));
   const bool nonfinite = amax >= 0x7F80u;  // an infinity or NaN in the block
   const uint32_t exp_field = amax >> 7;
   sbyte = nonfinite ? 0xFFu : (exp_field >= 8u ? exp_field - 8u : 0u);
   const float mult = __uint_as_float((254u - (nonfinite ? 127u : sbyte)) << 23);  // 2^(127 - sbyte), exact
-  const uint32_t c0 = fp8x2(__uint_as_float(w.x << 16) * mult, __uint_as_float(w.x & 0xFFFF0000u) * mult);
-  const uint32_t c1 = fp8x2(__uint_as_float(w.y << 16) * mult, __uint_as_float(w.y & 0xFFFF0000u) * mult);
-  const uint32_t c2 = fp8x2(__uint_as_float(w.z << 16) * mult, __uint_as_float(w.z & 0xFFFF0000u) * mult);
-  const uint32_t c3 = fp8x2(__uint_as_float(w.w << 16) * mult, __uint_as_float(w.w & 0xFFFF0000u) * mult);
-  const uint2 out = make_uint2(c0 | (c1 << 16), c2 | (c3 << 16));
-  return nonfinite ? make_uint2(0u, 0u) : out;
+  const uint4 out = make_uint4(bf16x2_e4m3x2(a.x, mult) | (bf16x2_e4m3x2(a.y, mult) << 16),
+                               bf16x2_e4m3x2(a.z, mult) | (bf16x2_e4m3x2(a.w, mult) << 16),
+                               bf16x2_e4m3x2(b.x, mult) | (bf16x2_e4m3x2(b.y, mult) << 16),
+                               bf16x2_e4m3x2(b.z, mult) | (bf16x2_e4m3x2(b.w, mult) << 16));
+  return nonfinite ? make_uint4(0u, 0u, 0u, 0u) : out;
 }
 
 // bf16 input: rows walked as in the fp32 form (whole rows per CTA, threads along
-// the row, 8 groups = 128 bytes of loads per thread before any is quantised),
-// with the row's bounds, addresses and scale-row offset computed once per row.
+// the row), each lane taking 16 consecutive elements (a lane pair holds one
+// 1x32 block) and 4 such units (128 bytes of loads) per step before any is
+// quantised; the row's bounds, addresses and scale-row offset are computed once
+// per row. The two 16-byte loads of a unit are adjacent, so a warp's pair of
+// load instructions covers 1 KB of the row exactly once.
 __device__ __forceinline__ void quantize_rows_bf16(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t K,
                                                    int64_t ldx, uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
-  constexpr int kU = 8;
-  const int k8 = static_cast<int>(K >> 3);  // 8-element groups per row (K < 2^31)
+  constexpr int kU = 4;
+  const int k16 = static_cast<int>(K >> 4);  // 16-element units per row (K < 2^31, a multiple of 8 units)
   const int64_t rows_pad = (rows + 127) & ~int64_t{127};
-  const unsigned quad = 0xFu << (threadIdx.x & 28u);
+  const unsigned pair = 0x3u << (threadIdx.x & 30u);
   const int bd = static_cast<int>(blockDim.x);
   for (int64_t r = blockIdx.x; r < rows_pad; r += gridDim.x) {
     uint8_t* sf_row = sf + ((r >> 7) * (K >> 7)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4;
     if (r >= rows) {  // padding row of the last 128-row scale block: scale 0x00, no codes
-      for (int c = threadIdx.x; c < (k8 >> 2); c += bd) sf_row[((c >> 2) << 9) + (c & 3)] = 0;
+      for (int c = threadIdx.x; c < (k16 >> 1); c += bd) sf_row[((c >> 2) << 9) + (c & 3)] = 0;
       continue;
     }
     const uint4* xr = reinterpret_cast<const uint4*>(x + r * ldx);
-    uint2* qr = reinterpret_cast<uint2*>(q + r * K);
-    for (int g0 = threadIdx.x; g0 < k8; g0 += bd * kU) {
-      uint4 raw[kU];
+    uint4* qr = reinterpret_cast<uint4*>(q + r * K);
+    auto emit = [&](const uint4 lo, const uint4 hi, int j) {
+      uint32_t sbyte;
+      qr[j] = quantize_bf16_half_block(lo, hi, pair, sbyte);
+      if ((j & 1) == 0) {
+        const int c = j >> 1;  // the 1x32 block
+        sf_row[((c >> 2) << 9) + (c & 3)] = static_cast<uint8_t>(sbyte);
+      }
+    };
+    int j0 = threadIdx.x;
+    // Whole steps: every unit of the step is inside the row (all of them when K
+    // is a multiple of 16 * blockDim * kU, e.g. K = 16384), no bounds checks.
+    const int full_end = k16 - (kU - 1) * bd;
+    for (; j0 < full_end; j0 += bd * kU) {
+      uint4 raw[2 * kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
-        const int g = g0 + u * bd;
-        raw[u] = g < k8 ? __ldcs(xr + g) : make_uint4(0u, 0u, 0u, 0u);
+        raw[2 * u] = __ldcs(xr + 2 * (j0 + u * bd));
+        raw[2 * u + 1] = __ldcs(xr + 2 * (j0 + u * bd) + 1);
       }
 #pragma unroll
+      for (int u = 0; u < kU; ++u) emit(raw[2 * u], raw[2 * u + 1], j0 + u * bd);
+    }
+    // The rest of the row (k16 and bd are even: a lane pair takes each branch together).
+    for (; j0 < k16; j0 += bd * kU) {
+      uint4 raw[2 * kU];
+#pragma unroll
       for (int u = 0; u < kU; ++u) {
-        const int g = g0 + u * bd;
-        if (g < k8) {  // k8 and bd are multiples of 4: a quad takes this branch together
-          uint32_t sbyte;
-          const uint2 codes = quantize_bf16_group(raw[u], quad, sbyte);
-          qr[g] = codes;
-          if ((g & 3) == 0) {
-            const int c = g >> 2;
-            sf_row[((c >> 2) << 9) + (c & 3)] = static_cast<uint8_t>(sbyte);
-          }
-        }
+        const int j = j0 + u * bd;
+        raw[2 * u] = j < k16 ? __ldcs(xr + 2 * j) : make_uint4(0u, 0u, 0u, 0u);
+        raw[2 * u + 1] = j < k16 ? __ldcs(xr + 2 * j + 1) : make_uint4(0u, 0u, 0u, 0u);
       }
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (j0 + u * bd < k16) emit(raw[2 * u], raw[2 * u + 1], j0 + u * bd);
     }
   }
 }
@@ -224,7 +247,9 @@ inline bool launch_quantize(const void* x, int dtype, int64_t rows, int64_t K, i
   const int64_t k8 = K >> 3;
   // Whole rows per CTA; threads along the row (a multiple of 32, at most 256).
   // One wave of resident CTAs, each walking a strided set of rows.
-  const int threads = static_cast<int>(k8 >= 256 ? 256 : ((k8 + 31) / 32) * 32);
+  // bf16 lanes take 16 elements each, fp32 lanes 8 per group.
+  const int64_t units = dtype == 0 ? k8 : k8 / 2;
+  const int threads = static_cast<int>(units >= 256 ? 256 : ((units + 31) / 32) * 32);
   static const int per_sm[2] = {resident_ctas(reinterpret_cast<const void*>(&mxfp8_quantize_kernel<0>), 256, 0),
                                 resident_ctas(reinterpret_cast<const void*>(&mxfp8_quantize_kernel<1>), 256, 0)};
   const int64_t wave = int64_t{sm_count} * per_sm[dtype == 0 ? 0 : 1];

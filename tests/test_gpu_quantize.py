@@ -23,7 +23,8 @@ def _run(x_np, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("rows,K", [(1, 128), (130, 256), (256, 1024), (1000, 384)])
+# K = 22528: whole 2048-group steps of 256 threads and a partial step in the same row.
+@pytest.mark.parametrize("rows,K", [(1, 128), (130, 256), (256, 1024), (1000, 384), (40, 22528), (3, 16384)])
 def test_quantize_bit_exact(dtype, rows, K):
     rng = np.random.default_rng(rows * 7 + K)
     x = O.make_square_source(rows, K, rng, zero_block_frac=0.05)
