@@ -82,6 +82,9 @@ def parse_args():
     p.add_argument("--qdtype", choices=("f32", "bf16"), default="f32", help="quantiser input type")
     p.add_argument("--measure-fp8-peak", action="store_true",
                    help="measure cuBLASLt MXFP8 (torch._scaled_mm) 8192^3: best-of-10 burst and 4 s sustained")
+    p.add_argument("--host-ceiling", action="store_true",
+                   help="measure the host-link ceiling of all ranks (concurrent pinned copies) and the phases of one "
+                        "end-to-end step (ShardedHostGemm at N > 1, HostGemm's copies at N = 1) instead of the GEMM")
     p.add_argument("--dist", choices=("square", "llm"), default="square",
                    help="input distribution: BASELINE square-sweep generator or LLM activations/weights")
     return p.parse_args()
@@ -1034,6 +1037,123 @@ def bench_configs(args, dev, stream):
     return out
 
 
+def bench_host_ceiling(args):
+    """What bounds the end-to-end rate: the host links of all ranks, and the phases of one step.
+
+    Every rank times, at the same time as the others (barrier, max over ranks):
+    512 MiB pinned host -> device, device -> host, and both directions at once
+    (two streams); then one rank alone. Then one end-to-end step at M, N, K and
+    each of its phases alone: at N > 1 ShardedHostGemm (this rank's rows of A in,
+    the NCCL all-gather of A, the B slice in, the GEMM, the D slice out); at
+    N = 1 the same copies and GEMM without the gather. Rank 0 prints one JSON line."""
+    import torch
+    import torch.distributed as dist
+
+    from cutex_b200.kernels import dense_gemm
+    from cutex_b200.kernels.dense_gemm_contract import scale_buffer_bytes
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def tmax(ms):
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    def timed(fn, reps=3):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return tmax(e0.elapsed_time(e1) / reps)
+
+    nb = 512 << 20
+    h_in = torch.empty(nb, dtype=torch.uint8).pin_memory()
+    h_out = torch.empty(nb, dtype=torch.uint8).pin_memory()
+    d_in = torch.empty(nb, dtype=torch.uint8, device=dev)
+    d_out = torch.zeros(nb, dtype=torch.uint8, device=dev)
+    side = torch.cuda.Stream(dev)
+
+    def both():
+        side.wait_stream(torch.cuda.current_stream())
+        d_in.copy_(h_in, non_blocking=True)
+        with torch.cuda.stream(side):
+            h_out.copy_(d_out, non_blocking=True)
+        torch.cuda.current_stream().wait_stream(side)
+
+    links = {
+        "h2d_GBs_all_ranks": world * nb / timed(lambda: d_in.copy_(h_in, non_blocking=True)) / 1e6,
+        "d2h_GBs_all_ranks": world * nb / timed(lambda: h_out.copy_(d_out, non_blocking=True)) / 1e6,
+        "both_directions_GBs_all_ranks": 2 * world * nb / timed(both) / 1e6,
+    }
+    one = timed(lambda: d_in.copy_(h_in, non_blocking=True) if rank == 0 else None)
+    links["h2d_GBs_one_rank_alone"] = nb / one / 1e6
+    del h_in, h_out, d_in, d_out
+
+    m, n, k = args.m, args.n, args.k
+    sfr = k // 32
+    phases = {}
+    if world > 1:
+        from cutex_b200.sharding import ShardedHostGemm
+
+        g = ShardedHostGemm(m, n, k)
+        r0, r1 = g.rows.n0, g.rows.n1
+        ha = torch.randint(0, 120, (r1 - r0, k), dtype=torch.uint8).pin_memory()
+        hsa = torch.full(((r1 - r0) * sfr,), 120, dtype=torch.uint8).pin_memory()
+        hb = torch.randint(0, 120, (g.cols.n, k), dtype=torch.uint8).pin_memory()
+        hsb = torch.full((g.sfb.numel(),), 120, dtype=torch.uint8).pin_memory()
+        hd = torch.empty(m, g.cols.n, dtype=torch.bfloat16).pin_memory()
+        g(ha, hsa, hb, hsb, hd)
+        phases["step_ms"] = timed(lambda: g(ha, hsa, hb, hsb, hd))
+        phases["a_rows_h2d_ms"] = timed(lambda: (g.a_part.copy_(ha.reshape(-1), non_blocking=True),
+                                                 g.sfa_part.copy_(hsa, non_blocking=True)))
+        phases["a_allgather_ms"] = timed(lambda: (dist.all_gather_into_tensor(g.a, g.a_part),
+                                                  dist.all_gather_into_tensor(g.sfa[: m * sfr], g.sfa_part)))
+        phases["b_h2d_ms"] = timed(lambda: (g.b.copy_(hb, non_blocking=True), g.sfb.copy_(hsb, non_blocking=True)))
+        phases["gemm_ms"] = timed(lambda: dense_gemm(g.a.view(m, k), g.b, g.sfa, g.sfb, g.d))
+        phases["d_d2h_ms"] = timed(lambda: hd.copy_(g.d, non_blocking=True))
+        host_bytes = world * sum(g.host_bytes())
+    else:
+        ha = torch.randint(0, 120, (m, k), dtype=torch.uint8).pin_memory()
+        hb = torch.randint(0, 120, (n, k), dtype=torch.uint8).pin_memory()
+        hsa = torch.full((scale_buffer_bytes(m, k),), 120, dtype=torch.uint8).pin_memory()
+        hsb = torch.full((scale_buffer_bytes(n, k),), 120, dtype=torch.uint8).pin_memory()
+        hd = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+        a, b = torch.empty_like(ha, device=dev), torch.empty_like(hb, device=dev)
+        sfa, sfb = torch.empty_like(hsa, device=dev), torch.empty_like(hsb, device=dev)
+        d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        phases["a_h2d_ms"] = timed(lambda: (a.copy_(ha, non_blocking=True), sfa.copy_(hsa, non_blocking=True)))
+        phases["b_h2d_ms"] = timed(lambda: (b.copy_(hb, non_blocking=True), sfb.copy_(hsb, non_blocking=True)))
+        phases["gemm_ms"] = timed(lambda: dense_gemm(a, b, sfa, sfb, d))
+        phases["d_d2h_ms"] = timed(lambda: hd.copy_(d, non_blocking=True))
+        host_bytes = ha.numel() + hb.numel() + hsa.numel() + hsb.numel() + hd.numel() * 2
+    flops = 2.0 * m * n * k
+    ceiling_ms = host_bytes / links["both_directions_GBs_all_ranks"] / 1e6
+    line = {"metric": "host-link ceiling and end-to-end step phases", "n_gpus": world,
+            "config": workload_config(m, n, k, world, args.dist), "links": links, "phases": phases,
+            "host_bytes_per_step": int(host_bytes),
+            "step_floor_ms_at_both_directions_rate": ceiling_ms,
+            "e2e_ceiling_tflops": flops / (ceiling_ms / 1e3) / 1e12}
+    if "step_ms" in phases:
+        line["e2e_one_stream_tflops"] = flops / (phases["step_ms"] / 1e3) / 1e12
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def measure_fp8_peak(args):
     """Dense FP8 denominator measured like the driver's BF16 peak: the vendor library on 8192^3.
 
@@ -1095,6 +1215,9 @@ def main():
         return
     if args.quantize is not None:
         bench_quantize(args)
+        return
+    if args.host_ceiling:
+        bench_host_ceiling(args)
         return
     if args.impl == "reference":
         bench_reference(args)

@@ -136,7 +136,58 @@ class GemmTrace:
                         per_role[role]["tile_boundary_gap_ns"] = {"mean": sum(gaps) / len(gaps), "max": max(gaps),
                                                                   "count": len(gaps)}
             result["ctas"][cta] = per_role
+        result["tile_handover_ns"] = self.tile_handover()
+        result["launch_edges_us"] = self.launch_edges()
         return result
+
+    def tile_handover(self) -> dict[str, float]:
+        """Medians over the traced pair's tile boundaries of the accumulator hand-over steps (ns).
+
+        last MMAs of tile i issued -> its accumulator seen full by the epilogue ->
+        the overlapping chunk read -> accumulator released -> first MMAs of tile
+        i + 1 issued."""
+
+        def by_tile(role, name):
+            return {e.tile: e.t_ns for e in self.events if e.cta == 0 and e.role == role and e.name == name}
+
+        done, go = by_tile("mma", "mma_tile_done"), by_tile("epilogue", "epi_go")
+        loaded, rel = by_tile("epilogue", "epi_loaded"), by_tile("epilogue", "epi_release")
+        acc_go = [(e.t_ns, e.tile) for e in self.events if e.cta == 0 and e.role == "mma" and e.name == "mma_acc_go"]
+        acc_go.sort()
+        nxt = {acc_go[i][1]: acc_go[i + 1][0] for i in range(len(acc_go) - 1)}  # tile -> next tile's start
+        steps = {"issued_to_full": [], "full_to_loaded": [], "loaded_to_released": [], "released_to_next_issue": []}
+        for t in done:
+            if t in go and t in loaded and t in rel and t in nxt:
+                steps["issued_to_full"].append(go[t] - done[t])
+                steps["full_to_loaded"].append(loaded[t] - go[t])
+                steps["loaded_to_released"].append(rel[t] - loaded[t])
+                steps["released_to_next_issue"].append(nxt[t] - rel[t])
+        out = {k: float(sorted(v)[len(v) // 2]) for k, v in steps.items() if v}
+        if out:
+            out["boundaries"] = len(steps["issued_to_full"])
+        return out
+
+    def launch_edges(self) -> dict[str, float]:
+        """Fill and drain of the launch (us): first CTA start to the traced pair's first loaded
+        stage and first issued MMAs, its last MMAs to its last stored tile, and the spread of
+        CTA starts."""
+
+        times = [(s, e) for s, e in self.cta_times if s and e]
+        ev = [e for e in self.events if e.cta == 0]
+        if not times or not ev:
+            return {}
+        t0 = min(s for s, _ in times)
+        first = lambda role, name: min((e.t_ns for e in ev if e.role == role and e.name == name), default=None)  # noqa: E731
+        last = lambda role, name: max((e.t_ns for e in ev if e.role == role and e.name == name), default=None)  # noqa: E731
+        out = {"cta_start_spread_us": (max(s for s, _ in times) - t0) / 1e3}
+        if first("mma", "mma_full_go") is not None:
+            out["start_to_first_loaded_stage_us"] = (first("mma", "mma_full_go") - self.cta_times[0][0]) / 1e3
+        if first("mma", "mma_issued") is not None:
+            out["start_to_first_mmas_issued_us"] = (first("mma", "mma_issued") - self.cta_times[0][0]) / 1e3
+        if last("mma", "mma_tile_done") is not None and last("epilogue", "epi_tile_done") is not None:
+            out["last_mmas_to_last_tile_stored_us"] = (last("epilogue", "epi_tile_done") -
+                                                      last("mma", "mma_tile_done")) / 1e3
+        return out
 
     def to_chrome_trace(self) -> dict[str, Any]:
         t0 = min((e.t_ns for e in self.events), default=0)
@@ -205,10 +256,50 @@ def run_gemm_trace(a, b, sfa, sfb, out, config=None, capacity: int = 1 << 16) ->
     return GemmTrace(events, capacity, (m, n, k), dict(cfg.__dict__), cta_times, cta_cycles)
 
 
+def main(argv=None) -> int:
+    """``python -m cutex_b200.trace --m M --n N --k K [--out DIR] [--config JSON]``: one traced launch.
+
+    Seeded N(0,1) operands quantised on the GPU by the library's quantiser; the
+    traced launch runs after one untimed traced warm-up launch; prints the
+    summary (per-CTA SM clock, end-of-launch spread, tile hand-over, launch
+    edges, per-role wait spans) as JSON and, with --out, writes the Chrome trace.
+    """
+
+    import argparse
+
+    import torch
+
+    from .kernels import GemmConfig, quantize_mxfp8
+
+    ap = argparse.ArgumentParser(description=main.__doc__.splitlines()[0])
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=16384)
+    ap.add_argument("--k", type=int, default=16384)
+    ap.add_argument("--config", default='{"kernel": 2, "stages": 6, "epi_buffers": 1, "sf_buffers": 1}')
+    ap.add_argument("--out", default=None)
+    args = ap.parse_args(argv)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a, sfa = quantize_mxfp8(torch.randn(args.m, args.k, device="cuda", generator=g))
+    b, sfb = quantize_mxfp8(torch.randn(args.n, args.k, device="cuda", generator=g))
+    d = torch.empty(args.m, args.n, dtype=torch.bfloat16, device="cuda")
+    cfg = GemmConfig(**json.loads(args.config))
+    run_gemm_trace(a, b, sfa, sfb, d, config=cfg)
+    tr = run_gemm_trace(a, b, sfa, sfb, d, config=cfg)
+    summary = tr.summary()
+    if args.out:
+        tr.write(args.out, stem=f"gemm_trace_m{args.m}_n{args.n}_k{args.k}")
+    print(json.dumps(summary, default=str))
+    return 0
+
+
 def disabled_trace_metadata() -> dict[str, Any]:
     """Result-metadata stanza for runs without tracing (same role as ``disabled_iket_metadata``)."""
 
     return {"enabled": False, "benchmark_instrumented": False, "tool": "cutex_mxfp8_gemm_trace"}
 
 
-__all__ = ["Event", "GemmTrace", "TraceError", "decode", "disabled_trace_metadata", "run_gemm_trace"]
+__all__ = ["Event", "GemmTrace", "TraceError", "decode", "disabled_trace_metadata", "main", "run_gemm_trace"]
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -45,6 +45,27 @@ def test_decode_and_summary_from_synthetic_records():
     assert disabled_trace_metadata()["benchmark_instrumented"] is False
 
 
+def test_tile_handover_and_launch_edges():
+    # Two tiles on the traced pair: tile 0's MMAs issued at 1000, its accumulator seen full
+    # at 1300, overlap chunk read at 1350, released at 1400, tile 1's MMAs start at 1500.
+    cap = 32
+    mma = [(500, 1, 0, 0), (500, 5, 0, 0), (520, 6, 0, 0), (600, 8, 0, 0), (700, 9, 0, 0), (1000, 10, 0, 0),
+           (1000, 5, 1, 0), (1500, 6, 1, 0), (1600, 8, 1, 0), (1700, 9, 1, 0), (2000, 10, 1, 0), (2100, 2, 0, 0)]
+    epi = [(500, 1, 0, 0), (500, 11, 0, 0), (1300, 12, 0, 0), (1350, 15, 0, 0), (1400, 13, 0, 0), (1900, 14, 0, 0),
+           (1900, 11, 1, 0), (2300, 12, 1, 0), (2350, 15, 1, 0), (2400, 13, 1, 0), (2900, 14, 1, 0)]
+    tr = GemmTrace(decode(_encode({(0, "mma"): mma, (0, "epilogue"): epi}, cap), cap), cap, (256, 512, 256),
+                   cta_times=[(400, 3000), (450, 2950)], cta_cycles=[(0, 1), (0, 1)])
+    h = tr.tile_handover()
+    assert h == {"issued_to_full": 300.0, "full_to_loaded": 50.0, "loaded_to_released": 50.0,
+                 "released_to_next_issue": 100.0, "boundaries": 1}
+    edges = tr.launch_edges()
+    assert edges["cta_start_spread_us"] == pytest.approx(0.05)
+    assert edges["start_to_first_loaded_stage_us"] == pytest.approx(0.2)
+    assert edges["start_to_first_mmas_issued_us"] == pytest.approx(0.3)
+    assert edges["last_mmas_to_last_tile_stored_us"] == pytest.approx(0.9)
+    assert tr.summary()["tile_handover_ns"]["boundaries"] == 1
+
+
 def test_sm_clock_from_cycle_counters():
     tr = GemmTrace([], 1, (1, 1, 1), cta_times=[(1000, 2000), (1000, 3000), (0, 0)],
                    cta_cycles=[(10, 1910), (5, 3805), (0, 0)])
