@@ -859,7 +859,7 @@ def time_quantizer(kind, qdtype, m, k, steps, warmup, dev, stream):
         graph.replay()
     torch.cuda.synchronize()
     sampler = ClockSampler(physical_gpu_index(dev.index or 0)).start()
-    time.sleep(0.1)
+    time.sleep(0.5)  # the same pause before the timed region as the GEMM's burst protocol
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler.mark()
     with torch.cuda.stream(stream):
@@ -909,7 +909,7 @@ def bench_quantize(args):
 # Other BASELINE configurations timed beside the headline in the default N = 1 run:
 # (name, M, N, K, input distribution, launches per timed region, L2 policy).
 SIDE_GEMMS = (
-    ("mxfp8_fprop_m4096_n4096_k4096", 4096, 4096, 4096, "square", 50, "flush"),
+    ("mxfp8_fprop_m4096_n4096_k4096", 4096, 4096, 4096, "square", 64, "rotate"),
     ("mxfp8_fprop_m8192_n28672_k8192", 8192, 28672, 8192, "llm", 20, "graph"),
     ("mxfp8_fprop_m128_n28672_k8192", 128, 28672, 8192, "llm", 200, "graph"),
     ("mxfp8_fprop_m16_n28672_k8192", 16, 28672, 8192, "llm", 200, "graph"),
@@ -936,11 +936,10 @@ def roofline_entry(flops, nbytes, ms, peaks, source):
 def bench_configs(args, dev, stream):
     """BASELINE's other configurations, each timed on the device in this run (N = 1).
 
-    GEMMs whose operands exceed the 126 MB L2 are timed as one CUDA graph of
-    back-to-back launches; 4096^3 (operands and D fit in L2) with a 256 MB L2
-    flush before every launch, as the difference of two graphs (with and
-    without the GEMMs). Each entry carries its clocks, kernel plan and roofline
-    fraction."""
+    Each is timed as one CUDA graph of back-to-back launches. GEMMs whose B
+    exceeds the 126 MB L2 run on one operand set; 4096^3 (operands and D fit in
+    the L2) cycles over enough operand sets to exceed twice the L2. Each entry
+    carries its clocks, kernel plan and roofline fraction."""
     import torch
 
     from cutex_b200 import _lib
@@ -950,69 +949,50 @@ def bench_configs(args, dev, stream):
     peaks, source = load_peaks()
     out = {}
     for name, m, n, k, dist, reps, policy in SIDE_GEMMS:
-        a, sfa, b, sfb = make_operands_on_device(m, n, k, 0, dev, dist)
-        d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        # "rotate": operands and D fit in the L2, so the launches cycle over `sets` operand
+        # sets whose bytes together exceed twice the 126 MB L2: every launch reads A and B
+        # that the launches in between have evicted. (A 256 MB write between launches
+        # leaves the whole L2 dirty, and the next GEMM pays for writing it back.)
+        per_set = m * k + n * k + (m + n) * (k // 32) + 2 * m * n
+        sets = max(1, -(-(2 * L2_FLUSH_BYTES) // per_set)) if policy == "rotate" else 1
         stream.wait_stream(torch.cuda.current_stream(dev))
+        steps, keep = [], []
+        for i in range(sets):
+            a, sfa, b, sfb = make_operands_on_device(m, n, k, 0, dev, dist)
+            d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+            stream.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(stream):
+                steps.append(PreparedGemm(a, b, sfa, sfb, d, stream=stream))
+            keep.append((a, sfa, b, sfb, d))
         with torch.cuda.stream(stream):
-            step = PreparedGemm(a, b, sfa, sfb, d, stream=stream)
             for _ in range(5):
-                step()
+                for st in steps:
+                    st()
         torch.cuda.synchronize()
         sampler = ClockSampler(physical_gpu_index(dev.index or 0)).start()
-        if policy == "graph":
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                for _ in range(reps):
-                    step()
-            with torch.cuda.stream(stream):
-                graph.replay()
-            torch.cuda.synchronize()
-            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            sampler.mark()
-            with torch.cuda.stream(stream):
-                s0.record(stream)
-                graph.replay()
-                s1.record(stream)
-            torch.cuda.synchronize()
-            sampler.close()
-            ms = s0.elapsed_time(s1) / reps
-            l2 = "no flush: B exceeds the 126 MB L2; one CUDA graph of back-to-back launches"
-            del graph
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(reps):
+                steps[i % sets]()
+        with torch.cuda.stream(stream):
+            graph.replay()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        time.sleep(0.5)  # the headline's burst protocol: a 0.5 s pause before each timed region
+        sampler.mark()
+        with torch.cuda.stream(stream):
+            s0.record(stream)
+            graph.replay()
+            s1.record(stream)
+        torch.cuda.synchronize()
+        sampler.close()
+        ms = s0.elapsed_time(s1) / reps
+        if sets > 1:
+            l2 = (f"inputs rotate over {sets} operand sets ({sets * per_set / 1e6:.0f} MB, over twice the 126 MB "
+                  "L2): every launch reads operands the launches in between evicted; one CUDA graph")
         else:
-            # Operands and D fit in the L2: a 256 MB write flushes it before every launch.
-            # One graph of `reps` x (flush, GEMM) and one of `reps` x flush, each timed as a
-            # whole (so no host gap enters a timed interval); the GEMM's time is the
-            # difference, median of three alternating rounds.
-            flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
-            g_both, g_flush = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g_both, stream=stream):
-                for _ in range(reps):
-                    flush.zero_()
-                    step()
-            with torch.cuda.graph(g_flush, stream=stream):
-                for _ in range(reps):
-                    flush.zero_()
-            with torch.cuda.stream(stream):
-                g_both.replay()
-                g_flush.replay()
-            torch.cuda.synchronize()
-
-            def timed(g):
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                with torch.cuda.stream(stream):
-                    e0.record(stream)
-                    g.replay()
-                    e1.record(stream)
-                torch.cuda.synchronize()
-                return e0.elapsed_time(e1)
-
-            sampler.mark()
-            diffs = sorted(timed(g_both) - timed(g_flush) for _ in range(3))
-            sampler.close()
-            ms = diffs[1] / reps
-            l2 = ("256 MB L2 flush before every launch: graph of (flush, GEMM) x launches minus graph of flush x "
-                  "launches, median of 3 rounds")
-            del g_both, g_flush, flush
+            l2 = "no flush: B exceeds the 126 MB L2; one CUDA graph of back-to-back launches"
+        del graph
         if _lib.load().cutex_last_device_status(stream.cuda_stream) != 0:
             raise RuntimeError(f"device-side timeout in {name}")
         flops = 2.0 * m * n * k
@@ -1024,7 +1004,7 @@ def bench_configs(args, dev, stream):
                  "l2": l2, "clocks": sampler.stop()}
         entry.update(roofline_entry(flops, nbytes, ms, peaks, source))
         out[name] = entry
-        del a, sfa, b, sfb, d, step
+        del keep, steps
         torch.cuda.empty_cache()
     for kind, qdtype in SIDE_QUANTIZERS:
         m = k = 16384
@@ -1069,6 +1049,7 @@ def bench_host_ceiling(args):
         return float(t[0])
 
     def timed(fn, reps=3):
+        fn()  # untimed first call: module loading, attributes, allocator
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()

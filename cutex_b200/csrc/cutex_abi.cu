@@ -362,13 +362,14 @@ struct Plan {
   int64_t ws_partials_bytes;  // offset of the counters inside the workspace
 };
 
-// Skinny stream-K workspace layout, fixed per device so that one workspace can
-// serve calls of any shape: a partial-sum region sized for the largest grid and
-// padded M (2 slots x sm_count CTAs x 128 x 128 fp32), then one uint32 arrival
-// counter per 128-row tile of B. Counters never alias partial slots, and every
-// completed call leaves the counters it used at zero.
-void skinny_workspace(int sm_count, int n_tiles, int64_t* partial_bytes, int64_t* total) {
-  *partial_bytes = static_cast<int64_t>(2) * sm_count * 128 * 128 * 4;
+// Skinny stream-K workspace layout, fixed per device and B-tiles-per-CTA-tile
+// count so that one workspace can serve calls of any shape: a partial-sum
+// region sized for the largest grid and padded M (2 slots x sm_count CTAs x
+// tiles x 128 x 128 fp32), then one uint32 arrival counter per CTA tile of B.
+// Counters never alias partial slots, and every completed call leaves the
+// counters it used at zero.
+void skinny_workspace(int sm_count, int n_tiles, int tiles, int64_t* partial_bytes, int64_t* total) {
+  *partial_bytes = static_cast<int64_t>(2) * sm_count * tiles * 128 * 128 * 4;
   *total = *partial_bytes + ((static_cast<int64_t>(n_tiles) * 4 + 255) / 256) * 256;
 }
 
@@ -438,13 +439,11 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
     // where whole tiles leave a second wave on 76 of 148 SMs (N = 28672).
     // Measured at N = 28672, K = 8192: M = 128 44.7 us vs 46.9 us whole,
     // M = 64 39.4 vs 41.8, M = 16 39.9 vs 40.5.
-    // Two 128-row B tiles per CTA tile (tile_n 256, whole tiles only): one A
-    // stage serves both tiles. Explicit only: measured at M = 64 / 128 it
-    // streams slower than single tiles (one wave of 112 CTAs).
+    // Two 128-row B tiles per CTA tile (tile_n 256): one A stage serves both
+    // tiles, stream-K or whole tiles as for single tiles.
     const int tiles = cfg.tile_n == 256 ? 2 : 1;
     SkinnyVariant* sv = find_skinny(M, tiles);
     if (sv == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;  // no double-tile build for this padded M
-    if (tiles == 2 && cfg.split_k > 1) return CUTEX_ERR_INVALID_ARGUMENT;
     if (cfg.stages != 0 && cfg.stages != sv->stages) return CUTEX_ERR_INVALID_ARGUMENT;
     plan->skinny = sv;
     plan->kernel = kernel;
@@ -455,13 +454,13 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
     plan->raster_group = 1;
     plan->raster_along_n = 0;
     const int64_t units = static_cast<int64_t>(plan->num_n_tiles) * (K / 128);
-    plan->streamk = (cfg.split_k == 1 || tiles == 2) ? 0 : 1;
+    plan->streamk = cfg.split_k == 1 ? 0 : 1;
     grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, plan->streamk ? units : plan->num_n_tiles)));
     plan->grid_ctas = grid;
     plan->dp_tiles = 0;
     if (plan->streamk && cfg.split_k == 3) plan->dp_tiles = plan->num_n_tiles / grid * grid;
     if (plan->streamk)
-      skinny_workspace(sm_count, plan->num_n_tiles, &plan->ws_partials_bytes, &plan->workspace_bytes);
+      skinny_workspace(sm_count, plan->num_n_tiles, tiles, &plan->ws_partials_bytes, &plan->workspace_bytes);
     return CUTEX_OK;
   }
   int tile_n = cfg.tile_n;
@@ -1103,6 +1102,7 @@ extern "C" int cutex_mxfp8_gemm_skinny_static(const void* a, const void* b, cons
 
   cutex_gemm_config cfg{};
   cfg.kernel = CUTEX_KERNEL_SKINNY;  // split_k = 0: stream-K over all SMs
+  cfg.tile_n = 128;                  // one 128-row B tile per CTA tile: the array holds one-tile slots
   Plan plan{};
   st = resolve_plan(&cfg, M, N, K, ds->sm_count, &plan);
   if (st != CUTEX_OK) return st;

@@ -18,7 +18,7 @@
 //
 // A CTA tile is kTiles x 128 rows of B (kTiles = 2: two MMAs per K-step share
 // the A stage, which halves A's L2 traffic and leaves more of the stage ring to
-// B; whole tiles only, since the split path's slots hold one 128-row tile).
+// B). A partial slot holds all kTiles 128-row tiles of a CTA tile.
 //
 // Warp roles (192 threads) as in the large kernel: warps 0-3 epilogue (TMEM lane
 // quarter w = rows 32w..32w+31 of each 128-row B tile), warp 4 MMA issuer,
@@ -44,7 +44,7 @@ struct SkinnyArgs {
   int dp_tiles;       // tiles [0, dp_tiles) whole, round-robin (stream-K mode)
   long long ldd;      // row stride of D (elements)
   __nv_bfloat16* d;
-  float* partials;    // [2 * gridDim.x][kNPad][128] fp32 slots (stream-K only)
+  float* partials;    // [2 * gridDim.x][kTiles][kNPad][128] fp32 slots (stream-K only)
   unsigned int* counters;  // [num_n_tiles] arrival counters, zero between calls
 };
 
@@ -303,8 +303,6 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t acc = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) +
                            static_cast<uint32_t>(buf ? C::kAcc1Col : 0);
       const bool whole = kb0 == 0 && kb1 == args.num_k_blocks;
-      if (!whole && kTiles != 1) atomicCAS(status, 0, kDevBadTile);  // the host never splits double tiles
-      const int n = tile * kTiles * 128 + static_cast<int>(tid);
       const int n0w = tile * kTiles * 128 + warp * 32;  // first D column of this warp's boxes
       // A tile cut between CTAs: the contributors of its K-range and whether all
       // the others have already published their slots. If so this CTA is the
@@ -314,7 +312,7 @@ __global__ void __launch_bounds__(192, 1)
       // so the result does not depend on which contributor finishes last.
       int c0 = 0, c1 = 0;
       bool early_last = false;
-      if (!whole && kTiles == 1) {
+      if (!whole) {
         const long long t_u0 = static_cast<long long>(tile - args.dp_tiles) * args.num_k_blocks;
         c0 = static_cast<int>(sk_owner(t_u0, P, U));
         c1 = static_cast<int>(sk_owner(t_u0 + args.num_k_blocks - 1, P, U));
@@ -326,21 +324,22 @@ __global__ void __launch_bounds__(192, 1)
         ptx::named_barrier(1, 128);
         early_last = slot[1] != 0u;
       }
-      auto slot_of = [&](int cc) {
+      // Contributor cc's slot, 128-row tile t of it: [kNPad / 4][128 rows][4 columns] fp32.
+      auto slot_of = [&](int cc, int t) {
         const int ft = args.dp_tiles + static_cast<int>(sk_start(cc, P, U) / args.num_k_blocks);
         const int s = (ft == tile) ? 2 * cc : 2 * cc + 1;
-        return reinterpret_cast<const float4*>(args.partials + static_cast<size_t>(s) * kNPad * 128);
+        return reinterpret_cast<const float4*>(args.partials + (static_cast<size_t>(s) * kTiles + t) * kNPad * 128);
       };
       constexpr int kPass = kNPad < 64 ? kNPad : 64;  // columns per reduction pass
       constexpr int kQ = kPass / 4;                    // float4 per thread per pass
-      auto store_row = [&](const float4 (&sum)[kQ], int c) {
+      auto store_row = [&](const float4 (&sum)[kQ], int c, int t) {
         if constexpr (kPass == 16) {
           float f[16];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             f[4 * q] = sum[q].x; f[4 * q + 1] = sum[q].y; f[4 * q + 2] = sum[q].z; f[4 * q + 3] = sum[q].w;
           }
-          skinny_emit<16, C::kEpiBufs>(f, dstage, dstage_addr, dbuf, lane, &tmap_d, n0w, c);
+          skinny_emit<16, C::kEpiBufs>(f, dstage, dstage_addr, dbuf, lane, &tmap_d, n0w + t * 128, c);
         } else {
 #pragma unroll
           for (int h = 0; h < kPass / 32; ++h) {
@@ -350,7 +349,7 @@ __global__ void __launch_bounds__(192, 1)
               const float4 x = sum[8 * h + q];
               f[4 * q] = x.x; f[4 * q + 1] = x.y; f[4 * q + 2] = x.z; f[4 * q + 3] = x.w;
             }
-            skinny_emit<32, C::kEpiBufs>(f, dstage, dstage_addr, dbuf, lane, &tmap_d, n0w, c + 32 * h);
+            skinny_emit<32, C::kEpiBufs>(f, dstage, dstage_addr, dbuf, lane, &tmap_d, n0w + t * 128, c + 32 * h);
           }
         }
       };
@@ -358,34 +357,37 @@ __global__ void __launch_bounds__(192, 1)
         __threadfence();
         const int nc = c1 - c0 + 1;
 #pragma unroll 1
-        for (int c = 0; c < kNPad; c += kPass) {
-          float4 sum[kQ];
+        for (int t = 0; t < kTiles; ++t) {
+#pragma unroll 1
+          for (int c = 0; c < kNPad; c += kPass) {
+            float4 sum[kQ];
 #pragma unroll
-          for (int q = 0; q < kQ; ++q) sum[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int i = 0; i < nc; ++i) {
-            float4 x[kQ];
-            if (c0 + i == static_cast<int>(blockIdx.x)) {
+            for (int q = 0; q < kQ; ++q) sum[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i = 0; i < nc; ++i) {
+              float4 x[kQ];
+              if (c0 + i == static_cast<int>(blockIdx.x)) {
 #pragma unroll
-              for (int h = 0; h < kPass / 16; ++h) {
-                uint32_t v[16];
-                ptx::tmem_ld_32x32b_x16(acc + c + 16 * h, v);
-                ptx::tmem_wait_ld();
+                for (int h = 0; h < kPass / 16; ++h) {
+                  uint32_t v[16];
+                  ptx::tmem_ld_32x32b_x16(acc + t * kNPad + c + 16 * h, v);
+                  ptx::tmem_wait_ld();
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                  x[4 * h + q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                                             __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                  for (int q = 0; q < 4; ++q)
+                    x[4 * h + q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                               __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                }
+              } else {
+                const float4* sx = slot_of(c0 + i, t);
+#pragma unroll
+                for (int q = 0; q < kQ; ++q) x[q] = __ldcg(sx + (c / 4 + q) * 128 + tid);
               }
-            } else {
-              const float4* sx = slot_of(c0 + i);
 #pragma unroll
-              for (int q = 0; q < kQ; ++q) x[q] = __ldcg(sx + (c / 4 + q) * 128 + tid);
+              for (int q = 0; q < kQ; ++q) {
+                sum[q].x += x[q].x; sum[q].y += x[q].y; sum[q].z += x[q].z; sum[q].w += x[q].w;
+              }
             }
-#pragma unroll
-            for (int q = 0; q < kQ; ++q) {
-              sum[q].x += x[q].x; sum[q].y += x[q].y; sum[q].z += x[q].z; sum[q].w += x[q].w;
-            }
+            store_row(sum, c, t);
           }
-          store_row(sum, c);
         }
         ptx::tc_fence_before();
         __syncwarp();
@@ -398,7 +400,7 @@ __global__ void __launch_bounds__(192, 1)
       float* part = nullptr;
       if (!whole) {
         const int s = (tile == first_tile) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
-        part = args.partials + static_cast<size_t>(s) * kNPad * 128;
+        part = args.partials + static_cast<size_t>(s) * kTiles * kNPad * 128;
       }
 #pragma unroll 1
       for (int t = 0; t < kTiles; ++t) {
@@ -430,22 +432,20 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t v[16];
           ptx::tmem_ld_32x32b_x16(acc + t * kNPad + c, v);
           ptx::tmem_wait_ld();
-          if (kTiles == 1) {
-            // Slot layout [kNPad / 4][128 rows][4 columns]: one 16-byte store per
-            // thread and column group, 512 contiguous bytes per warp.
-            float4* part4 = reinterpret_cast<float4*>(part);
+          // Slot layout per 128-row tile [kNPad / 4][128 rows][4 columns]: one 16-byte
+          // store per thread and column group, 512 contiguous bytes per warp.
+          float4* part4 = reinterpret_cast<float4*>(part + static_cast<size_t>(t) * kNPad * 128);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              part4[(c / 4 + q) * 128 + tid] =
-                  make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
-                              __uint_as_float(v[4 * q + 3]));
-          }
+          for (int q = 0; q < 4; ++q)
+            part4[(c / 4 + q) * 128 + tid] =
+                make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
+                            __uint_as_float(v[4 * q + 3]));
         }
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(acc_empty_bar(buf));
-      if (!whole && kTiles == 1) {
+      if (!whole) {
         // Publish the slot, count arrivals; the contributor that arrives last sums.
         __threadfence();
         ptx::named_barrier(1, 128);
@@ -460,14 +460,15 @@ __global__ void __launch_bounds__(192, 1)
           // in flight per step: the loop is latency-bound.
           const int nc = c1 - c0 + 1;
 #pragma unroll 1
-          for (int c = 0; c < kNPad; c += kPass) {
+          for (int tc = 0; tc < kTiles * kNPad; tc += kPass) {
+            const int t = tc / kNPad, c = tc % kNPad;  // kPass divides kNPad
             float4 sum[kQ];
 #pragma unroll
             for (int q = 0; q < kQ; ++q) sum[q] = make_float4(0.f, 0.f, 0.f, 0.f);
             int i = 0;
             for (; i + 1 < nc; i += 2) {
-              const float4* sx = slot_of(c0 + i);
-              const float4* sy = slot_of(c0 + i + 1);
+              const float4* sx = slot_of(c0 + i, t);
+              const float4* sy = slot_of(c0 + i + 1, t);
               float4 x[kQ], y[kQ];
 #pragma unroll
               for (int q = 0; q < kQ; ++q) x[q] = __ldcg(sx + (c / 4 + q) * 128 + tid);
@@ -480,7 +481,7 @@ __global__ void __launch_bounds__(192, 1)
               }
             }
             if (i < nc) {
-              const float4* sx = slot_of(c0 + i);
+              const float4* sx = slot_of(c0 + i, t);
               float4 x[kQ];
 #pragma unroll
               for (int q = 0; q < kQ; ++q) x[q] = __ldcg(sx + (c / 4 + q) * 128 + tid);
@@ -489,7 +490,7 @@ __global__ void __launch_bounds__(192, 1)
                 sum[q].x += x[q].x; sum[q].y += x[q].y; sum[q].z += x[q].z; sum[q].w += x[q].w;
               }
             }
-            store_row(sum, c);
+            store_row(sum, c, t);
           }
           if (tid == 0) args.counters[tile] = 0u;
         }

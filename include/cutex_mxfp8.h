@@ -130,8 +130,9 @@ typedef struct cutex_epilogue {
  *   cutex_mxfp8_query(...)->workspace_bytes, 256-byte aligned, zero-filled once
  *   before its first use (cudaMemsetAsync); every completed call leaves it
  *   ready for the next one, whatever the next call's shape (the layout is fixed
- *   per device: 2 * SMs * 64 KiB of partial sums, then 4 bytes per 128 rows of
- *   N of arrival counters). Calls that may overlap on the GPU need separate
+ *   per device and B tiles per CTA tile: 2 * SMs * tiles * 64 KiB of partial
+ *   sums, then 4 bytes per CTA tile of N of arrival counters; tile_n 256 on the
+ *   skinny kernel is two 128-row tiles). Calls that may overlap on the GPU need separate
  *   workspaces. With the AUTO kernel and no (or a too small) workspace, M <= 128
  *   runs without the split (whole 128-row tiles per CTA); an explicit
  *   CUTEX_KERNEL_SKINNY config without the workspace returns CUTEX_ERR_WORKSPACE.

@@ -87,6 +87,27 @@ def test_double_b_tiles(shape):
         _ok(check(run_gemm(a, sfa, b, sfb, M, N, K, cfg), a, sfa, b, sfb, M, N, K))
 
 
+@pytest.mark.parametrize("case", [(128, 2560, 2048, 7, 0), (100, 1280, 1024, 13, 3), (48, 4096, 1024, 0, 2),
+                                  (16, 1552, 4096, 5, 0), (128, 1296, 768, 3, 2), (64, 512, 8192, 0, 0)], ids=str)
+def test_double_b_tiles_stream_k(case):
+    # tile_n = 256 with the split: a CTA tile (two 128-row B tiles) cut between contributors
+    # goes through slots holding both tiles; ragged N leaves part of the second tile past N.
+    M, N, K, grid, split = case
+    a, sfa, b, sfb = make_operands(M, N, K, seed=M * 3 + N)
+    cfg = GemmConfig(kernel=SKINNY, tile_n=256, split_k=split, max_ctas=grid)
+    plan = query(M, N, K, cfg)
+    assert plan["tile_n"] == 256 and plan["split_k"] == 0 and plan["workspace_bytes"] > 0
+    for _ in range(2):  # the second call reuses the workspace the first left ready
+        _ok(check(run_gemm(a, sfa, b, sfb, M, N, K, cfg), a, sfa, b, sfb, M, N, K))
+
+
+def test_double_b_tiles_stream_k_llm_full_size():
+    M, N, K = 128, 28672, 8192
+    a, sfa, b, sfb = make_operands(M, N, K, seed=5, kind="llm")
+    cfg = GemmConfig(kernel=SKINNY, tile_n=256)
+    _ok(check(run_gemm(a, sfa, b, sfb, M, N, K, cfg), a, sfa, b, sfb, M, N, K))
+
+
 def test_whole_tile_mode():
     M, N, K = 128, 1280, 1024
     a, sfa, b, sfb = make_operands(M, N, K, seed=4)
