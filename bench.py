@@ -54,7 +54,9 @@ def parse_args():
     p.add_argument("--m", type=int, default=16384)
     p.add_argument("--n", type=int, default=16384)
     p.add_argument("--k", type=int, default=16384)
-    p.add_argument("--e2e-steps", type=int, default=6)
+    p.add_argument("--e2e-steps", type=int, default=12,
+                   help="end-to-end steps in the timed region (a stream of independent requests: more steps "
+                        "amortise the first step's uncovered H2D and the last step's uncovered D2H)")
     p.add_argument("--e2e-streams", type=int, default=2,
                    help="N = 1: independent steps alternate over this many streams, each with its own HostGemm "
                         "(device buffers) and pinned result, so one step's D2H overlaps the next step's H2D")
