@@ -211,6 +211,15 @@ __device__ __forceinline__ void tma_store_2d(const void* map, uint32_t src, int3
                : "memory");
 }
 
+// The same store with an L2 cache policy for the written lines.
+__device__ __forceinline__ void tma_store_2d_hint(const void* map, uint32_t src, int32_t x, int32_t y,
+                                                  uint64_t cache_hint) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y), "l"(cache_hint)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
