@@ -1,7 +1,10 @@
 """Benchmark: MXFP8 block-scaled GEMM TFLOPS on 1..8 B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cutex|reference]
-                    [--m M --n N --k K] [--allgather]
+                    [--m M --n N --k K] [--dist square|llm] [--config JSON]
+                    [--no-allgather] [--no-configs] [--vs-cublaslt ROUNDS]
+    python bench.py --quantize rowwise|columnwise [--qdtype f32|bf16]
+    python bench.py --host-ceiling        (under torchrun for N > 1)
 
 Workload (default): the reference's fixed contract M = N = K = 16384
 (BASELINE configs[2]); at N > 1 GPUs the GEMM is N-sharded (rank r computes
@@ -16,7 +19,10 @@ overlapped; independent steps alternate over ``--e2e-streams`` streams so one
 step's D2H overlaps the next step's H2D); on N GPUs through ``ShardedHostGemm``
 (each rank copies 1/N of A and its B slice in, A is all-gathered over NVLink,
 D slices come back in row blocks; steps alternate over ``--e2e-sharded-streams``
-streams, each with its own process group).
+streams, each with its own process group). At N > 1 the line also times gathering
+D on every rank, NCCL after the GEMM against the all-gather fused into the
+GEMM's epilogue (``allgather``); at N = 1 it carries cuBLASLt on the same
+operands (``vs_cublaslt``) and BASELINE's other configurations (``configs``).
 
 ``--impl reference`` times the contract's CPU path (dequantise, fp32 matmul,
 cast to BF16: the oracle port) on the host cores, on bounded row/column
@@ -501,7 +507,7 @@ def bench_cutex(args):
         if world > 1:
             dist.all_reduce(ts, op=dist.ReduceOp.MAX)
         sustained_value = 2.0 * m * n * k * launches / (float(ts[0]) / 1e3) / 1e12
-        peak_s, peak_s_src = fp8_peak(load_peaks()[0], load_peaks()[1], True)
+        peak_s, peak_s_src = fp8_peak(*load_peaks(), True)
         sustained = {"value": sustained_value, "unit": "TFLOP/s", "launches": launches,
                      "seconds": float(ts[0]) / 1e3, "clocks": clocks2,
                      "frac": sustained_value / world / peak_s, "peak": peak_s, "peak_source": peak_s_src}
