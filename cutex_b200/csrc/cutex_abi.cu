@@ -288,7 +288,7 @@ Variant make_variant() {
 // dynamic CLC scheduler, [instrumented twin]).
 Variant g_variants[] = {
     // dynamic (cluster launch control) scheduling: the default
-    make_variant<2, 256, 6, 1, 1, true, true, true>(), make_variant<2, 256, 5, 2, 1, true>(),
+    make_variant<2, 256, 6, 1, 1, true, true, true>(), make_variant<2, 256, 5, 2, 1, true, false, true>(),
     make_variant<2, 256, 6, 1, 2, true>(), make_variant<2, 256, 4, 2, 1, true>(),
     make_variant<2, 128, 6, 2, 1, true>(), make_variant<2, 128, 8, 1, 1, true>(),
     make_variant<1, 256, 4, 1, 1, true, true, true>(), make_variant<1, 256, 3, 2, 1, true>(),
