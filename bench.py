@@ -1090,6 +1090,29 @@ def bench_host_ceiling(args):
     }
     one = timed(lambda: d_in.copy_(h_in, non_blocking=True) if rank == 0 else None)
     links["h2d_GBs_one_rank_alone"] = nb / one / 1e6
+    # The host pipeline copies each finished D block (rows x cols of a row-major [M, N] D) back
+    # as a pitched 2-D copy: the same bytes as a 512 MiB contiguous copy, in 4096 x 4096 bf16
+    # blocks with the 16384-element row pitch of D.
+    try:
+        from cuda.bindings import runtime as cudart
+
+        pitch = 16384 * 2
+        rows_blk, cols_blk = 4096, 4096
+        nblk = nb // (rows_blk * cols_blk * 2)
+        kind = cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost
+
+        def pitched():
+            hs = torch.cuda.current_stream().cuda_stream
+            for i in range(nblk):
+                off = (i // 4) * rows_blk * pitch + (i % 4) * cols_blk * 2
+                err = cudart.cudaMemcpy2DAsync(h_out.data_ptr() + off, pitch, d_out.data_ptr() + off, pitch,
+                                               cols_blk * 2, rows_blk, kind, hs)[0]
+                if err != cudart.cudaError_t.cudaSuccess:
+                    raise RuntimeError(f"cudaMemcpy2DAsync: {err}")
+
+        links["d2h_pitched_blocks_GBs_all_ranks"] = world * nb / timed(pitched) / 1e6
+    except ImportError:
+        links["d2h_pitched_blocks_GBs_all_ranks"] = None
     del h_in, h_out, d_in, d_out
 
     m, n, k = args.m, args.n, args.k
