@@ -453,8 +453,8 @@ def bench_cutex(args):
             graph.replay()  # first replay outside the timed region
         torch.cuda.synchronize()
 
-    # The timed region starts after a 0.5 s pause (the burst protocol of every round of this
-    # bench); the 2 s back-to-back `sustained` entry below is the power-capped rate.
+    # The timed region starts after a 0.5 s pause (the bench's burst protocol); the 2 s
+    # back-to-back `sustained` entry below is the power-capped rate.
     sampler = ClockSampler(physical_gpu_index(local)).start()
     time.sleep(0.5)
     if world > 1:
