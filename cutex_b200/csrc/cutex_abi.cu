@@ -192,22 +192,23 @@ bool encode_output_fp8(CUtensorMap* map, void* p, int64_t M, int64_t N, int64_t 
 }
 
 // Columnwise quantiser input x [rows, cols] (fp32 or bf16, row stride ldx
-// elements) read in 128-row x 64-column boxes; columns past `cols` read as 0.
-bool encode_columnwise_input(CUtensorMap* map, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx) {
+// elements) read in 128-row x tile_cols-column boxes; columns past `cols` read as 0.
+bool encode_columnwise_input(CUtensorMap* map, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx,
+                             int tile_cols) {
   const uint64_t elem = dtype == 0 ? 4u : 2u;
   const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
   const uint64_t strides[1] = {static_cast<uint64_t>(ldx) * elem};
-  const uint32_t box[2] = {static_cast<uint32_t>(kColTileCols), static_cast<uint32_t>(kColTileRows)};
+  const uint32_t box[2] = {static_cast<uint32_t>(tile_cols), static_cast<uint32_t>(kColTileRows)};
   return encode(map, dtype == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims,
                 strides, box, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
 }
 
-// Columnwise quantiser output qt [cols, rows] e4m3 written in 64-row x
+// Columnwise quantiser output qt [cols, rows] e4m3 written in tile_cols-row x
 // 128-byte boxes with a 128-byte swizzle; rows past `cols` are clipped.
-bool encode_columnwise_output(CUtensorMap* map, void* qt, int64_t rows, int64_t cols) {
+bool encode_columnwise_output(CUtensorMap* map, void* qt, int64_t rows, int64_t cols, int tile_cols) {
   const uint64_t dims[2] = {static_cast<uint64_t>(rows), static_cast<uint64_t>(cols)};
   const uint64_t strides[1] = {static_cast<uint64_t>(rows)};
-  const uint32_t box[2] = {static_cast<uint32_t>(kColTileRows), static_cast<uint32_t>(kColTileCols)};
+  const uint32_t box[2] = {static_cast<uint32_t>(kColTileRows), static_cast<uint32_t>(tile_cols)};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qt, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_NONE);
 }
@@ -230,17 +231,17 @@ int launch_quantize_columnwise_t(const CUtensorMap& tmap, const CUtensorMap& tma
     if (per_sm_epoch[dev] != epoch) {
       if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
         return CUTEX_ERR_CUDA;
-      per_sm[dev] = resident_ctas(fn, 256, C::kSmemBytes);
+      per_sm[dev] = resident_ctas(fn, C::kThreads, C::kSmemBytes);
       per_sm_epoch[dev] = epoch;
     }
     resident = per_sm[dev];
   }
   const int64_t cols_pad = (cols + 127) & ~int64_t{127};
-  const int64_t num_tiles = (cols_pad / kColTileCols) * (rows / kColTileRows);
+  const int64_t num_tiles = (cols_pad / C::kCols) * (rows / kColTileRows);
   const int64_t wave = int64_t{sm_count} * resident;
   const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min(num_tiles, wave)));
-  mxfp8_quantize_columnwise_kernel<kDtype><<<blocks, 256, C::kSmemBytes, stream>>>(tmap, tmap_qt, rows, cols,
-                                                                                   static_cast<uint8_t*>(sft));
+  mxfp8_quantize_columnwise_kernel<kDtype><<<blocks, C::kThreads, C::kSmemBytes, stream>>>(
+      tmap, tmap_qt, rows, cols, static_cast<uint8_t*>(sft));
   return cudaGetLastError() == cudaSuccess ? CUTEX_OK : CUTEX_ERR_CUDA;
 }
 
@@ -981,7 +982,9 @@ extern "C" int cutex_mxfp8_quantize_columnwise(const void* x, int32_t x_dtype, i
   const int st = current_device_state(&ds);
   if (st != CUTEX_OK) return st;
   CUtensorMap tmap, tmap_qt;
-  if (!encode_columnwise_input(&tmap, x, x_dtype, rows, cols, ldx) || !encode_columnwise_output(&tmap_qt, qt, rows, cols))
+  const int tile_cols = x_dtype == 0 ? ColCfg<0>::kCols : ColCfg<1>::kCols;
+  if (!encode_columnwise_input(&tmap, x, x_dtype, rows, cols, ldx, tile_cols) ||
+      !encode_columnwise_output(&tmap_qt, qt, rows, cols, tile_cols))
     return CUTEX_ERR_CUDA;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return x_dtype == 0 ? launch_quantize_columnwise_t<0>(tmap, tmap_qt, rows, cols, sft, ds->sm_count, s)

@@ -5,15 +5,17 @@
 // the scales land in the 128x4 swizzled layout of a [cols, K = rows] operand.
 // Same per-block rule as the rowwise kernel (mxfp8_quant.cuh).
 //
-// Persistent CTAs (one wave) walk 128-row x 64-column tiles of x (column tiles
-// fastest). TMA brings each tile into a kStages-deep ring in shared memory
-// (dense rows; columns past `cols` read as zero), so kStages - 1 tiles are in
-// flight while one is quantised and no registers hold loads. Warp w takes
-// 32-row block w % 4 of tile columns 32 (w / 4) .. + 31: one lane per column
-// (consecutive lanes read consecutive words of a row: no bank conflicts), and
-// each lane holds a whole 32-element block (no shuffles). The codes go to a
-// [64 qt rows][128 bytes] staging tile (128-byte swizzle) that one TMA store
-// writes out, and the four scale bytes of a column leave as one 32-bit store.
+// Persistent CTAs (one wave) walk 128-row x kCols-column tiles of x (in
+// groups of kGroupRows row tiles, row tile fastest inside a group; kCols = 64
+// for fp32, 128 for bf16, so both read 256-byte row segments and 32 KB tiles). TMA brings each tile into a kStages-deep ring in
+// shared memory (dense rows; columns past `cols` read as zero), so kStages - 1
+// tiles are in flight while one is quantised and no registers hold loads. The
+// CTA has 4 kCols threads; warp w takes 32-row block w % 4 of tile columns
+// 32 (w / 4) .. + 31: one lane per column (consecutive lanes read consecutive
+// elements of a row: no bank conflicts), and each lane holds a whole
+// 32-element block (no shuffles). The codes go to a [kCols qt rows][128 bytes]
+// staging tile (128-byte swizzle) that one TMA store writes out, and the four
+// scale bytes of a column leave as one 32-bit store.
 // Columns from `cols` to the next multiple of 128 (the scale layout's padding
 // rows) get scale 0x00 and no element writes.
 #pragma once
@@ -27,33 +29,38 @@
 namespace cutex {
 
 constexpr int kColTileRows = 128;
-constexpr int kColTileCols = 64;
-// Ring depth per CTA: 2 fp32 tiles (32 KB each) or 3 bf16 tiles (16 KB each).
-// The kernel stalls mostly at its per-tile CTA barriers, so more CTAs per SM
-// with shallower rings beat fewer CTAs with deeper ones (measured at 16384^2:
-// 3 + 6 stages 234 / 161 us, 2 + 3 stages 230 / 155 us for fp32 / bf16).
-constexpr int kColStagesF32 = 2;
-constexpr int kColStagesBF16 = 3;
+// Ring depth per CTA: 2 tiles of 32 KB. The kernel stalls mostly at its
+// per-tile CTA barriers, so more CTAs per SM with shallower rings beat fewer
+// CTAs with deeper ones (fp32 at 16384^2: 3 stages 234 us, 2 stages 230 us).
+constexpr int kColStages = 2;
 
 template <int kDtype>  // 0: float32, 1: bfloat16
 struct ColCfg {
   static constexpr int kElemBytes = kDtype == 0 ? 4 : 2;
-  static constexpr int kTileBytes = kColTileRows * kColTileCols * kElemBytes;
-  static constexpr int kStages = kDtype == 0 ? kColStagesF32 : kColStagesBF16;
-  static constexpr int kOutBytes = kColTileCols * kColTileRows;  // E4M3 codes [64 qt rows][128]
-  static constexpr int kOffOut = 0;                               // 1024-aligned (128-byte swizzle)
+  static constexpr int kCols = kDtype == 0 ? 64 : 128;  // tile columns: 256-byte row segments
+  static constexpr int kThreads = 4 * kCols;             // one thread per (column, 32-row block)
+  static constexpr int kMinBlocks = kDtype == 0 ? 1 : 2;
+  // Row tiles per group in the tile order (tile_origin). Measured at 16384^2,
+  // in us for groups of 1 / 4 / 8 / 16 / 32 row tiles: fp32 234.6 / 231.5 /
+  // 234.3 / 241.4 / 247.0, bf16 153.4 / 150.1 / 149.0 / 147.1 / 149.3.
+  static constexpr int kGroupRows = kDtype == 0 ? 4 : 16;
+  static constexpr int kTileBytes = kColTileRows * kCols * kElemBytes;
+  static constexpr int kStages = kColStages;
+  static constexpr int kOutBytes = kCols * kColTileRows;  // E4M3 codes [kCols qt rows][128]
+  static constexpr int kOffOut = 0;                        // 1024-aligned (128-byte swizzle)
   static constexpr int kOffStages = kOffOut + kOutBytes;
-  static constexpr int kOffScales = kOffStages + kStages * kTileBytes;  // [64 columns][4 blocks]
-  static constexpr int kOffBar = kOffScales + kColTileCols * 4;
+  static constexpr int kOffScales = kOffStages + kStages * kTileBytes;  // [kCols columns][4 blocks]
+  static constexpr int kOffBar = kOffScales + kCols * 4;
   static constexpr int kSmemBytes = kOffBar + 8 * kStages + 1024;  // + base alignment slack
 };
 
 template <int kDtype>
-__global__ void __launch_bounds__(256) mxfp8_quantize_columnwise_kernel(const __grid_constant__ CUtensorMap tmap_x,
-                                                                        const __grid_constant__ CUtensorMap tmap_qt,
-                                                                        int64_t rows, int64_t cols,
-                                                                        uint8_t* __restrict__ sft) {
+__global__ void __launch_bounds__(ColCfg<kDtype>::kThreads, ColCfg<kDtype>::kMinBlocks)
+    mxfp8_quantize_columnwise_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                     const __grid_constant__ CUtensorMap tmap_qt, int64_t rows, int64_t cols,
+                                     uint8_t* __restrict__ sft) {
   using C = ColCfg<kDtype>;
+  constexpr int kCols = C::kCols;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = ptx::smem_u32(smem_raw);
   const uint32_t smem = (raw_base + 1023u) & ~1023u;
@@ -62,18 +69,32 @@ __global__ void __launch_bounds__(256) mxfp8_quantize_columnwise_kernel(const __
   int* status = &g_cutex_device_status;
 
   const int64_t cols_pad = (cols + 127) & ~int64_t{127};
-  const int64_t col_tiles = cols_pad / kColTileCols;
-  const int64_t num_tiles = col_tiles * (rows / kColTileRows);
+  const int64_t col_tiles = cols_pad / kCols;
+  const int64_t row_tiles = rows / kColTileRows;
+  const int64_t num_tiles = col_tiles * row_tiles;
   const int t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
   const int blk = warp & 3;                  // 32-row block of the tile
   const int lcol = (warp >> 2) * 32 + lane;  // column within the tile
 
+  // Tile u -> (first row, first column) of x. Tiles come in groups of
+  // kGroupRows row tiles; inside a group the row tile runs fastest, so the
+  // CTAs in flight together read a band of kGroupRows x 128 rows of x in runs
+  // of several KB and write runs of kGroupRows x 128 bytes of each qt row
+  // (with the column tile fastest, each qt row got 128-byte runs).
+  auto tile_origin = [&](int64_t u, int64_t& r0, int64_t& c0) {
+    const int64_t per_group = int64_t{C::kGroupRows} * col_tiles;
+    const int64_t g = u / per_group, w = u - g * per_group;
+    const int64_t rows_in_group = min(int64_t{C::kGroupRows}, row_tiles - g * C::kGroupRows);
+    r0 = (g * C::kGroupRows + w % rows_in_group) * kColTileRows;
+    c0 = (w / rows_in_group) * kCols;
+  };
   auto issue = [&](int64_t u, int s) {  // one thread: TMA of tile u into stage s
+    int64_t r0, c0;
+    tile_origin(u, r0, c0);
     ptx::mbar_arrive_expect_tx(full_bar(s), C::kTileBytes);
-    ptx::tma_load_2d(smem + C::kOffStages + s * C::kTileBytes, &tmap_x, full_bar(s),
-                     static_cast<int32_t>((u % col_tiles) * kColTileCols),
-                     static_cast<int32_t>((u / col_tiles) * kColTileRows), ptx::policy_evict_first());
+    ptx::tma_load_2d(smem + C::kOffStages + s * C::kTileBytes, &tmap_x, full_bar(s), static_cast<int32_t>(c0),
+                     static_cast<int32_t>(r0), ptx::policy_evict_first());
   };
   if (t == 0) {
     ptx::prefetch_tmap(&tmap_x);
@@ -96,15 +117,15 @@ __global__ void __launch_bounds__(256) mxfp8_quantize_columnwise_kernel(const __
     ok = ptx::mbar_wait(full_bar(s), static_cast<uint32_t>(i / C::kStages) & 1u, status, kDevTimeoutQuantize);
     ok = __syncthreads_and(ok) != 0;
     if (!ok) break;
-    const int64_t r0 = (u / col_tiles) * kColTileRows;
-    const int64_t c0 = (u % col_tiles) * kColTileCols;
+    int64_t r0, c0;
+    tile_origin(u, r0, c0);
     const int64_t c = c0 + lcol;  // output row of qt
     const uint8_t* stage = smem_ptr + C::kOffStages + s * C::kTileBytes;
     float v[32];
     uint32_t amax = 0u;  // magnitude bits: integer order is value order, NaN/inf the maximum
 #pragma unroll
     for (int k = 0; k < 32; ++k) {
-      const int idx = (blk * 32 + k) * kColTileCols + lcol;
+      const int idx = (blk * 32 + k) * kCols + lcol;
       if constexpr (kDtype == 0)
         v[k] = reinterpret_cast<const float*>(stage)[idx];
       else
@@ -144,7 +165,7 @@ __global__ void __launch_bounds__(256) mxfp8_quantize_columnwise_kernel(const __
       ptx::tma_store_2d(&tmap_qt, smem + C::kOffOut, static_cast<int32_t>(r0), static_cast<int32_t>(c0));
       ptx::bulk_commit_group();
     }
-    if (t < kColTileCols) {
+    if (t < kCols) {
       // Column c0 + t: its four blocks' scale bytes are 4 consecutive bytes of
       // the 128x4 layout (r0 / 32 is a multiple of 4).
       const int64_t cc = c0 + t;

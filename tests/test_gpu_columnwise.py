@@ -37,7 +37,9 @@ def _col(x_np, dtype, ldx=None):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("rows,cols", [(128, 64), (128, 1), (256, 200), (384, 130), (1024, 512), (128, 4100)])
+# (2176, 260): 17 row tiles, so the tile order's last group of row tiles is a partial one.
+@pytest.mark.parametrize("rows,cols", [(128, 64), (128, 1), (256, 200), (384, 130), (1024, 512), (128, 4100),
+                                       (2176, 260)])
 def test_columnwise_bit_exact(dtype, rows, cols):
     rng = np.random.default_rng(rows * 11 + cols)
     x = O.make_square_source(rows, cols, rng, zero_block_frac=0.0)
