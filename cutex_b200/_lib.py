@@ -2,15 +2,20 @@
 
 The library is loaded from ``cutex_b200/_lib`` (built in-tree by
 ``cutex_b200.build``). There is no fallback: if the library is missing or
-fails to load, every GEMM/quantiser call raises.
+fails to load, every GEMM/quantiser call raises. With ``CUTEX_B200_CHECKED=1``
+in the environment the checked build (``libcutex_mxfp8_checked.so``, device-side
+index checks in every kernel) is loaded instead.
 """
 
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 
-from .build import LIB_PATH
+from .build import CHECKED_LIB_PATH, LIB_PATH
+
+CHECKED_ENV = "CUTEX_B200_CHECKED"
 
 CUTEX_OK = 0
 CUTEX_ERR_INVALID_ARGUMENT = 1
@@ -137,6 +142,9 @@ SIGNATURES = {
     "cutex_mxfp8_quantize_columnwise": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
     "cutex_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "cutex_last_device_status": (ctypes.c_int, [_vp]),
+    "cutex_build_checked": (ctypes.c_int, []),
+    "cutex_device_check_record": (ctypes.c_int, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i64)]),
+    "cutex_selftest_device_check": (ctypes.c_int, [_vp]),
     "cutex_device_sm_count": (ctypes.c_int, [ctypes.POINTER(_i32)]),
     "cutex_version": (ctypes.c_char_p, []),
 }
@@ -150,12 +158,14 @@ def load() -> ctypes.CDLL:
         return _lib
     with _lock:
         if _lib is None:
-            if not LIB_PATH.exists():
+            checked = os.environ.get(CHECKED_ENV) == "1"
+            path = CHECKED_LIB_PATH if checked else LIB_PATH
+            if not path.exists():
                 raise RuntimeError(
-                    f"cutex_b200 native library not found at {LIB_PATH}; "
-                    "build it with `python -m cutex_b200.build` (there is no CPU fallback)"
+                    f"cutex_b200 native library not found at {path}; build it with "
+                    f"`python -m cutex_b200.build{' --checked' if checked else ''}` (there is no CPU fallback)"
                 )
-            lib = ctypes.CDLL(str(LIB_PATH))
+            lib = ctypes.CDLL(str(path))
             for name, (restype, argtypes) in SIGNATURES.items():
                 fn = getattr(lib, name)
                 fn.restype = restype
@@ -188,3 +198,14 @@ def make_config(**fields) -> GemmConfigC:
 
 def version() -> str:
     return load().cutex_version().decode()
+
+
+def check_record(stream=None) -> tuple[int, int]:
+    """(site code, offending value) of the failed device-side check that set the status word, then cleared.
+
+    (0, 0) when none failed; always (0, 0) in a build without checks."""
+
+    site, value = ctypes.c_int32(), ctypes.c_int64()
+    check(load().cutex_device_check_record(stream, ctypes.byref(site), ctypes.byref(value)),
+          "cutex_device_check_record")
+    return site.value, value.value

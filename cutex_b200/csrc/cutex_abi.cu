@@ -1021,6 +1021,39 @@ extern "C" int cutex_last_device_status(cutex_stream_t stream) {
   return CUTEX_OK;
 }
 
+namespace cutex {
+// One warp; lane 7 fails a check with a known value (no memory is accessed
+// apart from the status word and the check record).
+__global__ void device_check_selftest_kernel() {
+  dev_check(threadIdx.x != 7, kChkSelfTest, 0x5EED00 + static_cast<long long>(threadIdx.x));
+}
+}  // namespace cutex
+
+extern "C" int cutex_build_checked(void) { return kCheckedBuild ? 1 : 0; }
+
+extern "C" int cutex_device_check_record(cutex_stream_t stream, int32_t* site, int64_t* value) {
+  if (site == nullptr || value == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
+  if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return CUTEX_ERR_CUDA;
+  long long rec[2] = {0, 0};
+  if (cudaMemcpyFromSymbol(rec, g_cutex_check_record, sizeof(rec)) != cudaSuccess) return CUTEX_ERR_CUDA;
+  if (rec[0] != 0) {
+    const long long zero[2] = {0, 0};
+    if (cudaMemcpyToSymbol(g_cutex_check_record, zero, sizeof(zero)) != cudaSuccess) return CUTEX_ERR_CUDA;
+  }
+  *site = static_cast<int32_t>(rec[0]);
+  *value = static_cast<int64_t>(rec[1]);
+  return CUTEX_OK;
+}
+
+extern "C" int cutex_selftest_device_check(cutex_stream_t stream) {
+  if (!kCheckedBuild) return CUTEX_ERR_INVALID_ARGUMENT;
+  DeviceState* ds = nullptr;
+  const int st = current_device_state(&ds);
+  if (st != CUTEX_OK) return st;
+  device_check_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>();
+  return cudaGetLastError() == cudaSuccess ? CUTEX_OK : CUTEX_ERR_CUDA;
+}
+
 extern "C" int cutex_device_sm_count(int32_t* sm_count) {
   if (sm_count == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
   DeviceState* ds = nullptr;
@@ -1030,7 +1063,9 @@ extern "C" int cutex_device_sm_count(int32_t* sm_count) {
   return st;
 }
 
-extern "C" const char* cutex_version(void) { return "cutex-b200 0.1.0 sm_100a"; }
+extern "C" const char* cutex_version(void) {
+  return kCheckedBuild ? "cutex-b200 0.1.0 sm_100a checked" : "cutex-b200 0.1.0 sm_100a";
+}
 
 // ---------------------------------------------------------------------------
 // No-allocation entry point for the split-K skinny GEMM.

@@ -35,25 +35,11 @@
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
-#include "mxfp8_quant.cuh"  // sf_offset: the 128x4 scale layout
+#include "device_status.cuh"  // status word, DeviceError, dev_check
+#include "mxfp8_quant.cuh"    // sf_offset: the 128x4 scale layout
 #include "ptx.cuh"
 
 namespace cutex {
-
-// Device-side error word; the first kernel error (e.g. a wait timeout) wins.
-// The library is a single translation unit, so the header defines it.
-__device__ int g_cutex_device_status = 0;
-
-enum DeviceError : int {
-  kDevOk = 0,
-  kDevTimeoutProducer = 0x101,
-  kDevTimeoutMma = 0x102,
-  kDevTimeoutEpilogue = 0x103,
-  kDevTimeoutAccEmpty = 0x104,
-  kDevTimeoutScheduler = 0x105,
-  kDevTimeoutQuantize = 0x106,  // columnwise quantiser: a TMA tile never arrived
-  kDevBadTile = 0x201,  // a scheduled tile id outside [0, num_tiles): work stopped, nothing accessed
-};
 
 struct GemmArgs {
   int num_m_tiles;  // output tiles along M (tile rows = 128 * kCtaGroup)
@@ -527,6 +513,10 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
     while (ok && src.next(t, lane == 0, true, status)) {
       int mt, nt;
       tile_coords(t, args, mt, nt);
+      if (!dev_check(mt >= 0 && mt < args.num_m_tiles && nt >= 0 && nt < args.num_n_tiles, kChkTile, t)) {
+        ok = false;
+        break;
+      }
       const int a_row = mt * (128 * kCtaGroup) + static_cast<int>(rank) * 128;
       const int b_row = nt * kTileN + static_cast<int>(rank) * C::kLoadN;
       const int sfa_blk = a_row / 128;
@@ -611,6 +601,10 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
         tr.rec(kEvMmaAccGo, t, 0);
         ptx::tc_fence_after();
         const uint32_t d_t = tmem_base + (buf ? C::kAcc1Col : 0);
+        if (!dev_check((buf ? C::kAcc1Col : 0) + kTileN <= C::kTmemCols, kChkTmemCols, buf ? C::kAcc1Col : 0)) {
+          ok = false;
+          break;
+        }
         for (int kb = 0; kb < args.num_k_blocks; ++kb, ++kit) {
           const int s = static_cast<int>(kit % kStages);
           tr.rec(kEvMmaFullWait, t, kb);
@@ -620,12 +614,16 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
           }
           tr.rec(kEvMmaFullGo, t, kb);
           ptx::tc_fence_after();
+          const uint32_t sf_off = static_cast<uint32_t>(kit % kSFBufs) * C::kSFBufCols;
+          if (!dev_check(C::kSFBCol + sf_off + C::kSFBCols <= C::kTmemCols, kChkTmemCols, C::kSFBCol + sf_off)) {
+            ok = false;
+            break;
+          }
           if (ptx::elect_one()) {
             const uint32_t sa = smem + C::kOffA + s * C::kABytes;
             const uint32_t sb = smem + C::kOffB + s * C::kBBytes;
             const uint32_t ssfa = smem + C::kOffSFA + s * C::kSFABytes;
             const uint32_t ssfb = smem + C::kOffSFB + s * C::kSFBBytes;
-            const uint32_t sf_off = static_cast<uint32_t>(kit % kSFBufs) * C::kSFBufCols;
             const uint32_t sfa_t = tmem_base + C::kSFACol + sf_off;
             const uint32_t sfb_t = tmem_base + C::kSFBCol + sf_off;
             ptx::tmem_cp_32x128b_x4<kCtaGroup>(sfa_t, ptx::sf_chunk_desc(ssfa));
@@ -672,6 +670,7 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
     for (; src.next(t, lane == 0, true, status); ++it) {
       int mt, nt;
       tile_coords(t, args, mt, nt);
+      if (!dev_check(mt >= 0 && mt < args.num_m_tiles && nt >= 0 && nt < args.num_n_tiles, kChkTile, t)) break;
       const int m_row = mt * (128 * kCtaGroup) + static_cast<int>(rank) * 128 + warp * 32;
       const int n_col = nt * kTileN;
       const int buf = it & 1;
@@ -683,9 +682,20 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
       const uint32_t acc = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) +
                            static_cast<uint32_t>(buf ? C::kAcc1Col : 0);
       const int first = buf == 0 ? C::kFirstChunk0 : 0;
+      bool chunks_ok = true;
 #pragma unroll 1
       for (int i = 0; i < C::kChunks; ++i) {
         const int c = (first + i) % C::kChunks;
+        // Checked builds: the chunk's TMEM columns, and the store's origin inside
+        // D's padded extent (a TMA store may not start at a negative coordinate).
+        if (!dev_check((buf ? C::kAcc1Col : 0) + c * 64 + 64 <= C::kTmemCols, kChkTmemCols,
+                       (buf ? C::kAcc1Col : 0) + c * 64) ||
+            !dev_check(m_row >= 0 && m_row < args.num_m_tiles * 128 * kCtaGroup && n_col + c * 64 >= 0 &&
+                           n_col + c * 64 < args.num_n_tiles * kTileN,
+                       kChkStore, (static_cast<long long>(m_row) << 32) | static_cast<uint32_t>(n_col + c * 64))) {
+          chunks_ok = false;
+          break;
+        }
         uint32_t v0[32], v1[32];
         ptx::tmem_ld_32x32b_x32(acc + c * 64, v0);
         ptx::tmem_ld_32x32b_x32(acc + c * 64 + 32, v1);
@@ -730,7 +740,9 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
           if (row < ((args.M + 127) & ~127) && n0 < args.N) {
             const bool real = row < args.M;  // padding rows of the scale layout: 0x00
             const int64_t off = sf_offset(row, n0 >> 5, args.N);
-            *reinterpret_cast<uint16_t*>(args.d_scales + off) = static_cast<uint16_t>(real ? (s0 | (s1 << 8)) : 0u);
+            if (dev_check(off >= 0 && off + 2 <= static_cast<int64_t>((args.M + 127) & ~127) * (args.N >> 5),
+                          kChkScaleOffset, off))
+              *reinterpret_cast<uint16_t*>(args.d_scales + off) = static_cast<uint16_t>(real ? (s0 | (s1 << 8)) : 0u);
           }
         } else {
           const uint32_t row_addr = cbuf + slot * C::kCBufBytes + lane * 128u;
@@ -758,6 +770,7 @@ __global__ void __launch_bounds__(kDynamic ? 224 : 192, 1)
         }
         ++chunk_ctr;
       }
+      if (!chunks_ok) break;
       tr.rec(kEvEpiTileDone, t, 0);
     }
     if (lane == 0) ptx::bulk_wait_group_all();

@@ -24,6 +24,8 @@
 
 #include <cstdint>
 
+#include "device_status.cuh"
+
 namespace cutex {
 
 __host__ __device__ inline int64_t sf_offset(int64_t r, int64_t c, int64_t K) {
@@ -96,14 +98,17 @@ __device__ __forceinline__ void finish_group(const float (&v)[8], int64_t rows, 
       out.x = fp8x2(v[0] * mult, v[1] * mult) | (fp8x2(v[2] * mult, v[3] * mult) << 16);
       out.y = fp8x2(v[4] * mult, v[5] * mult) | (fp8x2(v[6] * mult, v[7] * mult) << 16);
     }
-    __stcs(reinterpret_cast<uint2*>(q + r * K + g * 8), out);  // streaming: written once, not read here
+    if (dev_check(r >= 0 && g >= 0 && g * 8 + 8 <= K, kChkCodeOffset, r * K + g * 8))
+      __stcs(reinterpret_cast<uint2*>(q + r * K + g * 8), out);  // streaming: written once, not read here
   }
   if ((g & 3) == 0) {
     // sf_offset(r, c = g / 4, K) with the row's part hoisted: 512-byte chunk
     // (r / 128, c / 4), byte (r % 32) * 16 + (r % 128 / 32) * 4 + c % 4.
     const int64_t row_part = ((r >> 7) * (K >> 7)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4;
     const uint32_t c = static_cast<uint32_t>(g) >> 2;
-    sf[row_part + ((c >> 2) << 9) + (c & 3u)] = static_cast<uint8_t>(sbyte);
+    const int64_t off = row_part + ((c >> 2) << 9) + (c & 3u);
+    if (dev_check(off >= 0 && off < ((rows + 127) & ~int64_t{127}) * (K >> 5), kChkScaleOffset, off))
+      sf[off] = static_cast<uint8_t>(sbyte);
   }
 }
 
@@ -151,18 +156,28 @@ __device__ __forceinline__ void quantize_rows_bf16(const __nv_bfloat16* __restri
   const int bd = static_cast<int>(blockDim.x);
   for (int64_t r = blockIdx.x; r < rows_pad; r += gridDim.x) {
     uint8_t* sf_row = sf + ((r >> 7) * (K >> 7)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4;
+    // Checked builds: every scale byte of the row inside the scale array.
+    const int64_t sf_row_off = sf_row - sf;
+    const int64_t sf_bytes = rows_pad * (K >> 5);
     if (r >= rows) {  // padding row of the last 128-row scale block: scale 0x00, no codes
-      for (int c = threadIdx.x; c < (k16 >> 1); c += bd) sf_row[((c >> 2) << 9) + (c & 3)] = 0;
+      for (int c = threadIdx.x; c < (k16 >> 1); c += bd) {
+        const int64_t off = ((c >> 2) << 9) + (c & 3);
+        if (dev_check(sf_row_off + off < sf_bytes, kChkScaleOffset, sf_row_off + off)) sf_row[off] = 0;
+      }
       continue;
     }
     const uint4* xr = reinterpret_cast<const uint4*>(x + r * ldx);
     uint4* qr = reinterpret_cast<uint4*>(q + r * K);
     auto emit = [&](const uint4 lo, const uint4 hi, int j) {
       uint32_t sbyte;
-      __stcs(qr + j, quantize_bf16_half_block(lo, hi, pair, sbyte));  // streaming: written once, not read here
+      const uint4 codes = quantize_bf16_half_block(lo, hi, pair, sbyte);
+      if (dev_check(j >= 0 && j < k16, kChkCodeOffset, r * K + 16 * static_cast<int64_t>(j)))
+        __stcs(qr + j, codes);  // streaming: written once, not read here
       if ((j & 1) == 0) {
         const int c = j >> 1;  // the 1x32 block
-        sf_row[((c >> 2) << 9) + (c & 3)] = static_cast<uint8_t>(sbyte);
+        const int64_t off = ((c >> 2) << 9) + (c & 3);
+        if (dev_check(sf_row_off + off < sf_bytes, kChkScaleOffset, sf_row_off + off))
+          sf_row[off] = static_cast<uint8_t>(sbyte);
       }
     };
     int j0 = threadIdx.x;

@@ -119,6 +119,12 @@ __global__ void __launch_bounds__(ColCfg<kDtype>::kThreads, ColCfg<kDtype>::kMin
     if (!ok) break;
     int64_t r0, c0;
     tile_origin(u, r0, c0);
+    // Checked builds: the tile inside x (rows) and the padded columns; the CTA
+    // leaves together (every thread computes the same origin).
+    if (!dev_check(r0 >= 0 && r0 + kColTileRows <= rows && c0 >= 0 && c0 + kCols <= cols_pad, kChkQuantTile, u)) {
+      ok = false;
+      break;
+    }
     const int64_t c = c0 + lcol;  // output row of qt
     const uint8_t* stage = smem_ptr + C::kOffStages + s * C::kTileBytes;
     float v[32];
@@ -169,9 +175,9 @@ __global__ void __launch_bounds__(ColCfg<kDtype>::kThreads, ColCfg<kDtype>::kMin
       // Column c0 + t: its four blocks' scale bytes are 4 consecutive bytes of
       // the 128x4 layout (r0 / 32 is a multiple of 4).
       const int64_t cc = c0 + t;
-      if (cc < cols_pad)
-        *reinterpret_cast<uint32_t*>(sft + sf_offset(cc, r0 >> 5, rows)) =
-            *reinterpret_cast<const uint32_t*>(smem_ptr + C::kOffScales + t * 4);
+      const int64_t off = sf_offset(cc, r0 >> 5, rows);
+      if (cc < cols_pad && dev_check(off >= 0 && off + 4 <= cols_pad * (rows >> 5), kChkScaleOffset, off))
+        *reinterpret_cast<uint32_t*>(sft + off) = *reinterpret_cast<const uint32_t*>(smem_ptr + C::kOffScales + t * 4);
     }
   }
   if (t == 0) ptx::bulk_wait_group_all();  // code stores complete before the CTA exits

@@ -215,6 +215,11 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t kit = 0;
       bool ok = true;
       while (ok && walk.next(args, tile, kb0, kb1)) {
+        if (!dev_check(tile >= 0 && tile < args.num_n_tiles && kb0 >= 0 && kb0 < kb1 && kb1 <= args.num_k_blocks,
+                       kChkSkinnySegment, (static_cast<long long>(tile) << 32) | static_cast<uint32_t>(kb0))) {
+          ok = false;
+          break;
+        }
         for (int kb = kb0; kb < kb1; ++kb, ++kit) {
           const int s = static_cast<int>(kit % kStages);
           if (!ptx::mbar_wait(empty_bar(s), ((kit / kStages) & 1u) ^ 1u, status, kDevTimeoutProducer)) {
@@ -252,6 +257,7 @@ __global__ void __launch_bounds__(192, 1)
           break;
         ptx::tc_fence_after();
         const uint32_t d_t = tmem_base + (buf ? C::kAcc1Col : 0);
+        if (!dev_check((buf ? C::kAcc1Col : 0) + C::kAccCols <= C::kSFCol, kChkTmemCols, buf ? C::kAcc1Col : 0)) break;
         for (int kb = kb0; kb < kb1; ++kb, ++kit) {
           const int s = static_cast<int>(kit % kStages);
           if (!ptx::mbar_wait(full_bar(s), (kit / kStages) & 1u, status, kDevTimeoutMma)) {
@@ -260,6 +266,11 @@ __global__ void __launch_bounds__(192, 1)
           }
           ptx::tc_fence_after();
           // Scale buffer: [B tile chunks 4 * kTiles columns | A chunk 4 columns].
+          if (!dev_check(C::kSFCol + (kit & 1u) * C::kSFBufCols + C::kSFBufCols <= C::kTmemCols, kChkTmemCols,
+                         C::kSFCol + (kit & 1u) * C::kSFBufCols)) {
+            ok = false;
+            break;
+          }
           const uint32_t sf_t = tmem_base + C::kSFCol + (kit & 1u) * C::kSFBufCols;
           const uint32_t sfa_t = sf_t + 4 * kTiles;
 #pragma unroll
@@ -316,6 +327,13 @@ __global__ void __launch_bounds__(192, 1)
         const long long t_u0 = static_cast<long long>(tile - args.dp_tiles) * args.num_k_blocks;
         c0 = static_cast<int>(sk_owner(t_u0, P, U));
         c1 = static_cast<int>(sk_owner(t_u0 + args.num_k_blocks - 1, P, U));
+        // Checked builds: the counter and every contributor's slot (2 c or 2 c + 1,
+        // c in [c0, c1]) inside the workspace. The same values in all 128
+        // threads, so the epilogue warps leave together, before any named barrier.
+        if (!dev_check(tile >= args.dp_tiles && tile < args.num_n_tiles && c0 >= 0 && c0 <= c1 && c1 < P &&
+                           c0 <= static_cast<int>(blockIdx.x) && static_cast<int>(blockIdx.x) <= c1,
+                       kChkWorkspace, (static_cast<long long>(c0) << 32) | static_cast<uint32_t>(c1)))
+          break;
         if (tid == 0) {
           unsigned int done;
           asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(done) : "l"(args.counters + tile) : "memory");

@@ -342,6 +342,31 @@ CUTEX_API const char* cutex_status_string(int status);
  */
 CUTEX_API int cutex_last_device_status(cutex_stream_t stream);
 
+/*
+ * Checked builds (libcutex_mxfp8_checked.so, compiled with -DCUTEX_CHECKED):
+ * every kernel also checks the indices it derives before it uses them (GEMM
+ * tile coordinates, TMEM column ranges, store origins inside D's padded extent,
+ * scale and code offsets, the skinny kernel's segments and workspace slots, the
+ * columnwise quantiser's tiles). A failed check faults nothing: the access is
+ * skipped, the kernel's roles leave their loops (the others stop at their
+ * bounded waits), and the status word reads CUTEX_ERR_DEVICE_CHECK. It stands
+ * in for an external memory checker such as compute-sanitizer's memcheck. The
+ * reference has no counterpart.
+ *
+ * cutex_build_checked: 1 for a checked build, 0 otherwise.
+ * cutex_device_check_record: synchronise `stream`, then read and clear the site
+ *   code (0x211-0x21F; 0 when no check failed) and the offending value of the
+ *   check that set the status word. The status word itself is read and cleared
+ *   by cutex_last_device_status.
+ * cutex_selftest_device_check: checked builds only (else
+ *   CUTEX_ERR_INVALID_ARGUMENT): launch one warp in which lane 7 fails a check
+ *   with value 0x5EED07 (site 0x21F), touching no memory but the status word and
+ *   the record.
+ */
+CUTEX_API int cutex_build_checked(void);
+CUTEX_API int cutex_device_check_record(cutex_stream_t stream, int32_t* site, int64_t* value);
+CUTEX_API int cutex_selftest_device_check(cutex_stream_t stream);
+
 /* Number of SMs and the library's build identifier (for autotune cache keys). */
 CUTEX_API int cutex_device_sm_count(int32_t* sm_count);
 CUTEX_API const char* cutex_version(void);

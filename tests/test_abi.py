@@ -33,6 +33,24 @@ def test_library_exports_every_declared_symbol():
     assert set(declared_functions()) == set(_lib.SIGNATURES)
 
 
+def test_checked_build_exports_the_same_abi():
+    """libcutex_mxfp8_checked.so (-DCUTEX_CHECKED) is built beside the product library
+    with the same entry points; only it reports itself as checked."""
+
+    from cutex_b200.build import CHECKED_LIB_PATH
+
+    checked = ctypes.CDLL(str(CHECKED_LIB_PATH))
+    for name in declared_functions():
+        assert hasattr(checked, name), name
+    checked.cutex_version.restype = ctypes.c_char_p
+    assert checked.cutex_build_checked() == 1 and checked.cutex_version().decode().endswith(" checked")
+    lib = _lib.load()
+    assert lib.cutex_build_checked() == 0 and not _lib.version().endswith("checked")
+    # The product build's self-test launches nothing; argument checks come before any CUDA call.
+    assert lib.cutex_selftest_device_check(None) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+    assert lib.cutex_device_check_record(None, None, None) == _lib.CUTEX_ERR_INVALID_ARGUMENT
+
+
 def test_struct_layouts_match_header():
     assert ctypes.sizeof(_lib.GemmConfigC) == 16 * 4
     assert ctypes.sizeof(_lib.GemmInfoC) == 14 * 4 + 8
