@@ -482,7 +482,17 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
     const int64_t n_tiles = ((M + 128 * cg - 1) / (128 * cg)) * ((N + tile_n - 1) / tile_n);
     if (n_tiles <= sm_count / cg) dynamic = 0;
   }
-  Variant* v = find_variant(cg, tile_n, cfg.stages, cfg.epi_buffers, cfg.sf_buffers, dynamic);
+  int stages = cfg.stages, epi_buffers = cfg.epi_buffers;
+  if (plain && cg == 2 && tile_n == 256 && stages == 0 && epi_buffers == 0 && cfg.sf_buffers == 0 && K >= 16384) {
+    // Long K: a 5-stage ring with two epilogue buffers per warp. Measured on two
+    // boxes (graphs of back-to-back launches, alternating): +0.5-0.9 % at K = 16384
+    // (16384^3, 8192^2 x 16384, 8192 x 28672 x 16384, 16384 x 2048 x 16384) and
+    // +3 % at 16384^2 x 32768; at K = 8192 and below the 6-stage ring with one
+    // buffer is 0.2-1.3 % faster.
+    stages = 5;
+    epi_buffers = 2;
+  }
+  Variant* v = find_variant(cg, tile_n, stages, epi_buffers, cfg.sf_buffers, dynamic);
   if (v == nullptr) return CUTEX_ERR_INVALID_ARGUMENT;
   plan->variant = v;
   plan->kernel = kernel;
