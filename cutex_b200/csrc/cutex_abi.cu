@@ -504,6 +504,19 @@ int resolve_plan(const cutex_gemm_config* cfg_in, int64_t M, int64_t N, int64_t 
   plan->num_tiles = static_cast<int>(tiles);
   plan->raster_group = cfg.raster_group != 0 ? cfg.raster_group : 8;
   plan->raster_along_n = cfg.raster_along_n;
+  if (cfg.raster_group == 0 && cg == 2 && tile_n == 256) {
+    // Library choice of both: the group spans the dimension with fewer tiles
+    // and walks the longer one, so the short side's panels (kept evict-last)
+    // serve the whole walk and the long side's stream through once; 16 tiles
+    // wide at K <= 8192, 8 above (about the same panel bytes). Measured
+    // (TFLOP/s, graphs of back-to-back launches, against 8 tiles walking M):
+    // 16384 x 2048 x 16384 2977 vs 2736, 16384 x 4096 x 16384 2954 vs 2844,
+    // 16384 x 8192 x 16384 2949 vs 2916, 2048 x 16384 x 16384 2968 vs 2965
+    // (walking N: 2729), 8192 x 28672 x 8192 3002 vs 2903, 8192^3 2921 vs 2841;
+    // 16384^3 unchanged (2965), 4096^3 insensitive.
+    plan->raster_along_n = plan->num_n_tiles < plan->num_m_tiles ? 1 : 0;
+    plan->raster_group = K <= 8192 ? 16 : 8;
+  }
   if (v->dynamic) {
     // One cluster per tile; resident clusters cancel and take over pending ones.
     plan->grid_ctas = plan->num_tiles * cg;

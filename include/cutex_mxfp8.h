@@ -65,8 +65,10 @@ typedef struct cutex_gemm_config {
   int32_t kernel;         /* CUTEX_KERNEL_* */
   int32_t tile_n;         /* 128 or 256 output columns per MMA tile */
   int32_t stages;         /* shared-memory ring depth */
-  int32_t raster_group;   /* output tiles per rasterisation group (>= 1) */
-  int32_t raster_along_n; /* 0: walk M inside a group, 1: walk N inside a group */
+  int32_t raster_group;   /* output tiles per rasterisation group (>= 1; 0 = library choice of the
+                             group and of raster_along_n) */
+  int32_t raster_along_n; /* 0: walk M inside a group, 1: walk N inside a group (used when
+                             raster_group is set) */
   int32_t split_k;        /* skinny kernel: 0 = stream-K over all SMs, 1 = whole tiles,
                              2 = stream-K over all SMs, 3 = whole tiles for the full waves +
                              stream-K remainder */

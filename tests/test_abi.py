@@ -74,6 +74,23 @@ def gemm(a=FAKE, b=FAKE, sfa=FAKE, sfb=FAKE, d=FAKE, M=256, N=256, K=256, ldd=25
     return _lib.load().cutex_mxfp8_gemm(a, b, sfa, sfb, d, M, N, K, ldd, ctypes.byref(c), ws, wsb, None)
 
 
+def test_default_raster_group_follows_k():
+    """CTA pairs, library choice: 16-tile groups at K <= 8192, 8 above; explicit groups are kept."""
+
+    lib = _lib.load()
+
+    def group(m, n, k, **cfg):
+        info = _lib.GemmInfoC()
+        c = _lib.make_config(**cfg)
+        assert lib.cutex_mxfp8_query(ctypes.byref(c), m, n, k, ctypes.byref(info)) == 0
+        return info.raster_group
+
+    assert group(16384, 2048, 16384) == 8
+    assert group(8192, 28672, 8192) == 16
+    assert group(8192, 28672, 8192, raster_group=4) == 4
+    assert group(4096, 4096, 4096, kernel=1, tile_n=128) == 8
+
+
 @pytest.mark.parametrize(
     "kwargs,status",
     [
