@@ -162,7 +162,8 @@ class ClockSampler:
     ``mark()`` opens and ``close()`` ends the window that ``stop()`` summarises
     (host ``perf_counter`` times bracketing the device-timed region: the host
     enqueues the region's work after ``mark()`` and returns from the final
-    synchronisation before ``close()``), so a 60 ms region gets its own samples.
+    synchronisation before ``close()``), so a region of a few ms (20 steps of a
+    rank's slice at 8 GPUs: ~7 ms) gets its own samples.
     Without ``nvidia_ml_py`` it falls back to ``nvidia-smi -lms 200``. Nothing is
     ever set through NVML.
     """
@@ -170,7 +171,7 @@ class ClockSampler:
     REASONS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
                ("hw_thermal_slowdown", 0x40), ("hw_power_brake_slowdown", 0x80))
 
-    def __init__(self, gpu_index: int, period_s: float = 0.01):
+    def __init__(self, gpu_index: int, period_s: float = 0.002):
         self.gpu_index = gpu_index
         self.period_s = period_s
         self.samples: list[tuple[float, float, float, float, int]] = []  # (t, sm MHz, max MHz, W, reasons)
