@@ -115,10 +115,12 @@ class FusedAllGatherGemm:
         self.num_peers = self.world - 1
         for i in range(self.BUFFERS):
             peers = []
-            for r, exported in enumerate(everyone):
-                if r == self.rank:
-                    continue
-                h, off = exported[i]
+            # Peers in rotated order (rank + 1, rank + 2, ...): each chunk's j-th peer
+            # store goes to a different GPU on every rank, so no GPU's ingress gets
+            # every rank's first store at once.
+            for j in range(1, self.world):
+                r = (self.rank + j) % self.world
+                h, off = everyone[r][i]
                 ptr, mapping = ctypes.c_void_p(), ctypes.c_void_p()
                 _lib.check(lib.cutex_ipc_import(h, off, ctypes.byref(ptr), ctypes.byref(mapping)),
                            "cutex_ipc_import")
