@@ -143,13 +143,15 @@ __device__ __forceinline__ uint4 quantize_bf16_half_block(const uint4 a, const u
 
 // bf16 input: rows walked as in the fp32 form (whole rows per CTA, threads along
 // the row), each lane taking 16 consecutive elements (a lane pair holds one
-// 1x32 block) and 4 such units (128 bytes of loads) per step before any is
+// 1x32 block) and 2 such units (64 bytes of loads) per step before any is
 // quantised; the row's bounds, addresses and scale-row offset are computed once
-// per row. The two 16-byte loads of a unit are adjacent, so a warp's pair of
+// per row. (At 16384^2: 2 units per step, 47 registers, 138.5-139.3 us; 4 units,
+// 64 registers and fewer resident CTAs, 141.1-141.5 us; 8 units, 110 registers,
+// 157 us; 1 unit 139.0-139.5 us.) The two 16-byte loads of a unit are adjacent, so a warp's pair of
 // load instructions covers 1 KB of the row exactly once.
 __device__ __forceinline__ void quantize_rows_bf16(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t K,
                                                    int64_t ldx, uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
-  constexpr int kU = 4;
+  constexpr int kU = 2;
   const int k16 = static_cast<int>(K >> 4);  // 16-element units per row (K < 2^31, a multiple of 8 units)
   const int64_t rows_pad = (rows + 127) & ~int64_t{127};
   const unsigned pair = 0x3u << (threadIdx.x & 30u);
